@@ -1,0 +1,318 @@
+#!/usr/bin/env python
+"""Benchmark: Gemma 4 E2B vision tower throughput (images/s) on B200.
+
+Step = one pass of the vision tower (patch embed, 16 encoder layers, 3x3
+pooler, embedder) over a batch of 64 seeded 768x768 images per GPU (the
+batched-vision configuration; weak scaling, one process per GPU under
+torchrun, no data-path collective).  Weights are random-init with the
+reference's dtypes (int8 QAT linears, BF16 norms / patch projection, F32
+embedder); inputs are U[0,1] pixels.
+
+`value` is device-timed (CUDA events on the launching stream, inputs resident
+in HBM, max over ranks); `e2e` is the same metric through the C ABI with
+pinned host buffers (host->device pixels and device->host embeddings inside
+the timed region).  `--impl reference` times the CPU restatement of the
+reference's CPU path (the oracle) on a bounded sample instead.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+PKG = "gemma-4-webgpu-kernels-multimodal_b200"
+
+HIDDEN, FF, HEADS, HD, TEXT = 768, 3072, 12, 64, 1536
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def weights_path(layers: int, rank: int, barrier) -> str:
+    syn = importlib.import_module(PKG + ".synthetic")
+    d = os.path.join(os.environ.get("TMPDIR", "/tmp"), "g4m_bench")
+    os.makedirs(d, exist_ok=True)
+    p = os.path.join(d, f"vision{layers}_seed0.safetensors")
+    if rank == 0 and not os.path.exists(p):
+        tmp = p + f".tmp{os.getpid()}"
+        syn.write_safetensors(tmp, syn.vision_weights(0, layers=layers))
+        os.replace(tmp, p)
+    barrier()
+    return p
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str):
+        self.uuid = uuid
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9 and self.uuid and self.uuid in parts[0]:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def measured_peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return {}
+
+
+def vision_kernel_flops(B: int, N: int, tokens: int):
+    """Algorithmic FLOPs per launch of each profiled kernel (2*M*N*K for a
+    linear, 4*n^2*d per head for attention), counted once (not per split
+    term)."""
+    M = B * N
+    return {
+        "gemm_qkv": 2.0 * M * 3 * HIDDEN * HIDDEN,
+        "gemm_o": 2.0 * M * HIDDEN * HIDDEN,
+        "gemm_gate_up": 2.0 * M * 2 * FF * HIDDEN,
+        "gemm_down": 2.0 * M * FF * HIDDEN,
+        "attention": 4.0 * B * HEADS * N * N * HD,
+        "gemm_patch": 2.0 * M * HIDDEN * 768,
+        "gemm_embed": 2.0 * B * tokens * TEXT * HIDDEN,
+    }
+
+
+def cpu_vision_sample(threads: int):
+    """Oracle (CPU restatement of the reference's CPU twins) on one 768x768
+    image: patch embedding + one encoder layer + pooler/embedder, scaled to
+    16 layers.  Returns (seconds per image, description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    syn = importlib.import_module(PKG + ".synthetic")
+    O.set_threads(threads)
+    W = syn.vision_weights(0, layers=1)
+    pix = syn.image_pixels(0, 768, 768)
+    pre = O.preprocess_image_pixels(pix)
+    patches, pos = O.valid_image_patch_input(pre)
+    t0 = time.perf_counter()
+    h = O.vision_patch_embeddings(W, patches, pos)
+    t1 = time.perf_counter()
+    h = O.vision_layer(W, 0, h, pos)
+    t2 = time.perf_counter()
+    pooled = O.vision_pooler(h, pos, 256)
+    O.embedder(pooled, W["model.embed_vision.embedding_projection.weight"])
+    t3 = time.perf_counter()
+    per_image = (t1 - t0) + 16 * (t2 - t1) + (t3 - t2)
+    return per_image, "1 image 768x768: patch embed + 1 of 16 encoder layers (x16) + pooler/embedder"
+
+
+def run_reference(args):
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    secs = []
+    desc = ""
+    for i in range(args.warmup + args.steps):
+        s, desc = cpu_vision_sample(threads)
+        if i >= args.warmup:
+            secs.append(s)
+    value = len(secs) / sum(secs)
+    line = {
+        "impl": "reference", "metric": "images/s (vision tower 768x768, 16 layers, + embedder)", "value": value,
+        "unit": "images/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * sum(secs) / len(secs), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (JS number / Math.fround semantics)", "data": "synthetic",
+        "config": {"workload": "vision batch, 768x768 images, 16 layers, reference CPU path (bounded sample)",
+                   "image": "768x768", "layers": 16},
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+
+    rank, world, local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    native = importlib.import_module(PKG + "._native")
+    syn = importlib.import_module(PKG + ".synthetic")
+    B, H, Wd, layers, max_soft = args.batch, 768, 768, 16, 280
+    N, tokens = (H // 16) * (Wd // 16), 256
+    path = weights_path(layers, rank, barrier)
+    ctx = native.Context([local])
+    ctx.load_weights(path)
+
+    pix_host = torch.empty((B, H, Wd, 3), dtype=torch.float32).pin_memory()
+    for i in range(B):
+        pix_host[i] = torch.from_numpy(syn.image_pixels(rank * B + i, H, Wd))
+    pix = pix_host.cuda()
+    out = torch.empty((B * tokens, TEXT), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step():
+        ctx.vision_embed_device(pix.data_ptr(), B, H, Wd, out.data_ptr(), max_soft, layers, stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    uuid = str(torch.cuda.get_device_properties(local).uuid)
+    clocks = ClockSampler(uuid)
+    clocks.start()
+    launches0 = native.kernel_launches()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    launches = native.kernel_launches() - launches0
+    ms = e0.elapsed_time(e1)
+    barrier()
+    clk = clocks.stop()
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = world * B * args.steps / (ms_max / 1000.0)
+
+    # roofline of the dominant kernel: per-launch CUDA-event times of one step
+    ctx.profile_begin()
+    step()
+    prof = ctx.profile_end()
+    flops = vision_kernel_flops(B, N, tokens)
+    dom = max((k for k in prof if k in flops), key=lambda k: prof[k][1])
+    cnt, tot = prof[dom]
+    peaks = measured_peaks()
+    peak = peaks.get("bf16_tflops_sustained")
+    peak_src = "measured (bf16 cuBLAS, sustained)" if peak else "fallback"
+    if not peak:
+        peak = 1400.0
+    achieved = flops[dom] / (tot / cnt / 1000.0) / 1e12
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic_per_launch.json")))
+        traffic = tr.get(dom, {}).get("bytes_per_launch_b64") if B == 64 else None
+    except Exception:
+        pass
+    roofline = {"bound": "tensor", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
+                "launch_ms": tot / cnt, "flop_per_launch": flops[dom]}
+    kernel_ms = {k: round(v[1], 4) for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
+
+    # end to end through the C ABI with pinned host buffers
+    out_host = [np.empty((tokens, TEXT), np.float32) for _ in range(B)]
+    out_pin = torch.empty((B, tokens, TEXT), dtype=torch.float32).pin_memory()
+    out_host = [out_pin[i].numpy() for i in range(B)]
+    in_host = [pix_host[i].numpy() for i in range(B)]
+    ctx.vision_embed(in_host, max_soft, layers, outs=out_host)
+    barrier()
+    k_e2e = max(1, min(args.steps, 5))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(k_e2e):
+        ctx.vision_embed(in_host, max_soft, layers, outs=out_host)
+    t_e2e = time.perf_counter() - t0
+    te = torch.tensor([t_e2e], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = world * B * k_e2e / float(te.item())
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        s, desc = cpu_vision_sample(threads)
+        cpu = {"value": 1.0 / s, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc}
+
+    if rank == 0:
+        line = {
+            "impl": "g4m", "metric": "images/s (vision tower 768x768, 16 layers, + embedder)", "value": value,
+            "unit": "images/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32-grade (fp16 hi/lo split operands on tcgen05, f32 accumulate)",
+            "data": "synthetic (seeded U[0,1] pixels, random-init weights with the reference dtypes)",
+            "config": {"workload": f"batched vision: {B} images/GPU of 768x768 (2304 patches, 256 tokens), 16 layers",
+                       "images_per_gpu": B, "image": "768x768", "layers": layers, "parallelism": f"dp{world} (replicas)",
+                       "l2": "inputs larger than L2 (pixels %.0f MB per GPU per step)" % (B * H * Wd * 3 * 4 / 1e6)},
+            "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": B * H * Wd * 3 * 4,
+                    "d2h_bytes_per_step": B * tokens * TEXT * 4},
+            "gpu_launches": launches,
+            "roofline": roofline,
+            "kernel_ms_per_step": kernel_ms,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if dist:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=64, help="images per GPU per step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,124 @@
+// Internal kernel launch interface of the g4m library (not the public C ABI;
+// that is include/g4m.h).  All launchers are asynchronous on `st`.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace g4m {
+
+enum Epi : int {
+  EPI_F32 = 0,         // y = srq(acc * row_scale * col_scale[n], s_out) (+ bias[n]) -> f32
+  EPI_GELU_GATE = 2,   // tile halves (gate | up) -> gelu_tanh(gate) * up -> fp16 hi/lo
+  EPI_SILU = 3,        // silu(srq(acc * s_w)) -> fp16 hi/lo
+  EPI_GLU = 4,         // tile halves (value | gate) -> value * sigmoid(gate) -> f32
+  EPI_QKV_VISION = 5,  // head RMSNorm + 2-D RoPE + attention layouts (fp16 hi/lo)
+  EPI_PATCH = 6,       // acc + pos_x row + pos_y row -> f32
+};
+
+struct GemmOperands {
+  const __half* a_hi;  // [M, K]
+  const __half* a_lo;  // [M, K] (terms >= 2)
+  const __half* b_hi;  // [N, K]
+  const __half* b_lo;  // [N, K] (terms == 3)
+};
+
+struct GemmArgs {
+  int M, N, K;
+  const float* col_scale;  // [N] per-output-channel weight scale (may be null for EPI_F32)
+  float row_scale;         // 1, or s_in when A holds integer codes
+  float s_out, s_out_b, s_out_c;
+  const float* bias;       // [N] or null
+  float* out_f32;
+  long ldo;
+  __half* out_hi;
+  __half* out_lo;
+  long ldh;
+  // EPI_QKV_VISION
+  int proj_width;          // 768: columns of one of q / k / v
+  int heads;
+  float eps;
+  const float* qn_w;       // [64]
+  const float* kn_w;       // [64]
+  const float* rope_cs;    // [rows_per_image][32] (cos, sin) pairs
+  __half *q_hi, *q_lo, *k_hi, *k_lo, *vt_hi, *vt_lo;
+  // EPI_QKV_VISION / EPI_PATCH
+  int rows_per_image;
+  int vt_pitch;            // row pitch (keys) of V^T, a multiple of 64
+  const int* pos_xy;       // [rows_per_image][2]
+  const float* posx_rows;  // [P][N]
+  const float* posy_rows;  // [P][N]
+  int* err;                // device error word
+};
+
+cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args, cudaStream_t st,
+                        int max_ctas = 0);
+bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+// Any cols with a 16-byte-multiple row pitch `pitch_elems` (>= cols).
+bool make_tmap_f16_any(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                       uint32_t box_rows);
+
+cudaError_t prep_a(const float* x, long rows, int cols, float s_in, const float* row_scale, __half* hi, __half* lo,
+                   cudaStream_t st);
+cudaError_t prep_w(const void* src, int kind, int bits, int rows, int cols, const int* map, __half* hi, __half* lo,
+                   cudaStream_t st);
+
+// ---------------------------------------------------------------------------
+// Row kernels (norms, residuals) -- kernels_rows.cu
+// ---------------------------------------------------------------------------
+struct RowArgs {
+  long rows;
+  int d;
+  float eps;
+  const float* y;          // optional: delta to normalise (w_post) and add
+  const float* w_post;     // RMSNorm weight applied to y (null: y added raw)
+  float res_scale;         // h += res_scale * norm(y)
+  const float* h_in;       // residual input (null: h = norm(y) or y)
+  const float* w_out;      // optional RMSNorm of the new residual (audio norm_out)
+  float* h_out;            // residual output (may alias h_in)
+  const float* w_next;     // optional RMSNorm producing the next GEMM operand
+  float s_in_next;         // srq of the next operand (0 = identity)
+  __half* a_hi;
+  __half* a_lo;
+  long lda;
+};
+cudaError_t fused_rows(const RowArgs& r, cudaStream_t st);
+
+// Vision helpers -- kernels_vision.cu
+cudaError_t vision_patch_operand(const float* pixels, int n_images, int height, int width, int patch, __half* hi,
+                                 __half* lo, cudaStream_t st);
+cudaError_t vision_pool_operand(const float* h, const int* pool_idx, int n_images, int rows_per_image, int tokens,
+                                int k2, int d, float eps, float* pooled_out, __half* hi, __half* lo, cudaStream_t st);
+cudaError_t vision_attention_simt(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
+                                  const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
+                                  __half* o_hi, __half* o_lo, cudaStream_t st);
+cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
+                                const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
+                                __half* o_hi, __half* o_lo, int* err, cudaStream_t st);
+
+// Audio helpers -- kernels_audio.cu
+struct AudioClipRows {
+  const int* row_clip;     // [rows] clip id of each packed row
+  const int* clip_row0;    // [clips] first packed row of each clip
+  const int* clip_rows;    // [clips] valid rows of each clip
+};
+cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
+                         const int* frames, int clips, int total_frames, const float* window, const float* mel,
+                         const float2* twiddle, float* features, uint8_t* mask, cudaStream_t st);
+cudaError_t audio_subsample_l0(const float* feats, const uint8_t* mask, const int* frame_off, const int* frames,
+                               const int* t0_off, const int* t0_len, int clips, int total_t0, const float* w,
+                               const float* nw, float eps, float* out, uint8_t* out_mask, cudaStream_t st);
+cudaError_t audio_subsample_l1(const float* in0, const uint8_t* mask0, const int* t0_off, const int* t0_len,
+                               const int* t1_off, const int* t1_len, int clips, int total_t1, const float* w,
+                               const float* nw, float eps, float* out, cudaStream_t st);
+cudaError_t audio_attention(const float* qkv, const float* relk, const float* pds, AudioClipRows cr, long rows,
+                            int heads, int hd, int chunk, int ctx, int plen, float softcap, __half* o_hi,
+                            __half* o_lo, cudaStream_t st);
+cudaError_t audio_lconv(const float* g, const float* dw, const float* nw, AudioClipRows cr, long rows, int d, int ks,
+                        float eps, float s_in_next, __half* a_hi, __half* a_lo, cudaStream_t st);
+cudaError_t gather_rows(const float* src, const int* rows_idx, long n, int d, float* dst, cudaStream_t st);
+cudaError_t row_inv_rms_operand(const float* x, long rows, int d, float eps, __half* hi, __half* lo, cudaStream_t st);
+cudaError_t add_bias_rows(float* y, const float* b, long rows, int d, cudaStream_t st);
+
+}  // namespace g4m

@@ -1,0 +1,592 @@
+// tcgen05 GEMM for the QAT / F32 / BF16 linears of the Gemma 4 E2B media
+// towers, with the reference's per-channel math fused into the epilogue.
+//
+// Replaces, on the device:
+//   runQatI8LinearWebGpu       src/kernels/qat.ts:601-759 (CPU twin 458-487)
+//   runPackedQatLinearWebGpu   src/kernels/qat.ts:263-432 (CPU twin 215-247)
+//   runF32LinearRowsWebGpu     src/kernels/qat.ts:35-157  (CPU twin 6-33)
+//   runVisionPatchEmbeddingWebGpu src/vision/kernels.ts:1021-1194 (matmul part)
+//   and, fused into epilogues, runVisionMlpActivationWebGpu, runSiluActivationWebGpu,
+//   runGluActivationWebGpu, the q/k/v head RMSNorm and runVisionRopeWebGpu.
+//
+// D[M,N] = sum over terms of A_t[M,K] * B_t[N,K]^T, fp16 operands, f32
+// accumulation in tensor memory.  Activations are carried as two fp16
+// planes (hi = fp16(x), lo = fp16(x - hi)), so one QAT linear is
+// hi*W + lo*W (int8 / unsigned-code weights are exact in fp16) and an F32
+// linear adds hi*W_lo: fp32-grade results from the fp16 tensor path.
+//
+// Kernel structure (one CTA per SM, persistent over output tiles):
+//   warp 0       TMA producer (one elected lane), STAGES-deep smem ring
+//   warp 1       TMEM owner + MMA issuer (one lane), 2 accumulator buffers
+//   warps 2..5   epilogue: TMEM -> registers -> fused math -> global
+// Every wait is bounded; a timeout records an error word and the CTA
+// unwinds, drains its own in-flight copies and frees its TMEM.
+#include "g4m_kernels.h"
+#include "g4m_sm100.cuh"
+#include "runtime_internal.h"
+
+#include <algorithm>
+#include <mutex>
+
+namespace g4m {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kGemmThreads = 192;
+
+template <int BN, int TERMS>
+struct GemmCfg {
+  static constexpr int NA = TERMS >= 2 ? 2 : 1;
+  static constexpr int NB = TERMS == 3 ? 2 : 1;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
+  static constexpr int STAGES = (196608 / STAGE_BYTES) > 6 ? 6 : (196608 / STAGE_BYTES);
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int TMEM_COLS = 2 * BN;
+};
+
+__device__ __forceinline__ float js_round_f(float x) {
+  float f = floorf(x);
+  return (x - f >= 0.5f) ? f + 1.0f : f;
+}
+
+// srqScalar (src/kernels/qat.ts:489-492): clamp(round(v/s), -128, 127) * s.
+__device__ __forceinline__ float srq_f(float v, float s) {
+  if (s == 0.0f) return v;
+  float r = js_round_f(__fdiv_rn(v, s));
+  r = fminf(fmaxf(r, -128.0f), 127.0f);
+  return r * s;
+}
+
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  // geluPytorchTanh, src/vision/kernels.ts:155-159
+  float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return 0.5f * x * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ void store_f16x2_row(__half* hi, __half* lo, const float* v, int n) {
+  // n multiple of 8; hi/lo 16-byte aligned
+  for (int j = 0; j < n; j += 8) {
+    __align__(16) __half h[8], l[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) split_f16(v[j + u], h[u], l[u]);
+    *reinterpret_cast<uint4*>(hi + j) = *reinterpret_cast<uint4*>(h);
+    *reinterpret_cast<uint4*>(lo + j) = *reinterpret_cast<uint4*>(l);
+  }
+}
+
+template <int BN, int TERMS, int EPI>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
+                   const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1, GemmArgs a) {
+  using C = GemmCfg<BN, TERMS>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[C::STAGES], bar_empty[C::STAGES], bar_accf[2], bar_acce[2];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag, skip;
+
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_n = a.N / BN, tiles_m = (a.M + BM - 1) / BM, tiles = tiles_m * tiles_n;
+  const int kblocks = a.K / BK;
+
+  if (threadIdx.x == 0) skip = *reinterpret_cast<volatile int*>(a.err) != 0;
+  __syncthreads();
+  if (skip) return;  // an earlier kernel on this device already failed
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_accf[b], 1);
+      mbar_init(&bar_acce[b], 4);
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&mA0);
+    prefetch_tmap(&mB0);
+    if (C::NA == 2) prefetch_tmap(&mA1);
+    if (C::NB == 2) prefetch_tmap(&mB1);
+  }
+  if (warp == 1) tmem_alloc(&tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_slot;
+
+  auto sA = [&](int s, int t) { return smem + s * C::STAGE_BYTES + t * C::A_BYTES; };
+  auto sB = [&](int s, int t) { return smem + s * C::STAGE_BYTES + C::NA * C::A_BYTES + t * C::B_BYTES; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        const int mb = tile / tiles_n, nb = tile % tiles_n;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t r = it / C::STAGES;
+          if (!mbar_wait(&bar_empty[s], (r & 1) ^ 1, a.err, kErrWaitEmpty, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&bar_full[s], C::STAGE_BYTES);
+          tma_load_2d(sA(s, 0), &mA0, &bar_full[s], kb * BK, mb * BM);
+          if (C::NA == 2) tma_load_2d(sA(s, 1), &mA1, &bar_full[s], kb * BK, mb * BM);
+          tma_load_2d(sB(s, 0), &mB0, &bar_full[s], kb * BK, nb * BN);
+          if (C::NB == 2) tma_load_2d(sB(s, 1), &mB1, &bar_full[s], kb * BK, nb * BN);
+        }
+      }
+      // Drain: the last use of every stage must have landed before exit.
+      const uint32_t first = it > (uint32_t)C::STAGES ? it - C::STAGES : 0;
+      for (uint32_t j = first; j < it; ++j) {
+        const uint32_t b = smem_u32(&bar_full[j % C::STAGES]);
+        const long long t0 = clock64();
+        while (!mbar_try_wait(b, (j / C::STAGES) & 1)) {
+          if (clock64() - t0 > kWaitCycles) {
+            atomicCAS(a.err, 0, kErrWaitDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+      uint32_t it = 0, t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++t) {
+        const uint32_t buf = t & 1, use = t >> 1;
+        if (!mbar_wait(&bar_acce[buf], (use & 1) ^ 1, a.err, kErrWaitAccEmpty, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t r = it / C::STAGES;
+          if (!mbar_wait(&bar_full[s], r & 1, a.err, kErrWaitFull, &abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA(s, 0)), b0 = smem_u32(sB(s, 0));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t da0 = desc_k_sw128(a0 + k * 32), db0 = desc_k_sw128(b0 + k * 32);
+            mma_f16_ss(d, da0, db0, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            if (TERMS >= 2) mma_f16_ss(d, desc_k_sw128(smem_u32(sA(s, 1)) + k * 32), db0, idesc, 1u);
+            if (TERMS == 3) mma_f16_ss(d, da0, desc_k_sw128(smem_u32(sB(s, 1)) + k * 32), idesc, 1u);
+          }
+          mma_commit(&bar_empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&bar_accf[buf]);
+      }
+      // Let the last stage-release commits land before the CTA can exit.
+      if (ok && !abort_flag) {
+        const uint32_t first = it > (uint32_t)C::STAGES ? it - C::STAGES : 0;
+        for (uint32_t j = first; j < it; ++j)
+          if (!mbar_wait(&bar_empty[j % C::STAGES], (j / C::STAGES) & 1, a.err, kErrWaitDrain, &abort_flag)) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row_in_tile = 32 * q + lane;
+    uint32_t t = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
+      const uint32_t buf = t & 1, use = t >> 1;
+      // tcgen05.ld is warp-collective: every lane takes the same branch.
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[buf], use & 1, a.err, kErrWaitAccFull, &abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const int mb = tile / tiles_n, nb = tile % tiles_n;
+      const uint32_t tb = tmem_base + ((uint32_t)(32 * q) << 16) + buf * BN;
+      const int row = mb * BM + row_in_tile;
+      const bool valid = row < a.M;
+      const float rs = a.row_scale;
+
+      if (EPI == EPI_F32 || EPI == EPI_PATCH) {
+        const int* pxy = (EPI == EPI_PATCH && valid) ? a.pos_xy + 2 * (size_t)(row % a.rows_per_image) : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tb + c * 32, v);
+          if (valid) {
+            const int n0 = nb * BN + c * 32;
+            float* dst = a.out_f32 + (size_t)row * a.ldo + n0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float y = v[j];
+              if (EPI == EPI_F32) {
+                if (a.col_scale) y = (y * rs) * a.col_scale[n0 + j];
+                y = srq_f(y, a.s_out);
+                if (a.bias) y = y + a.bias[n0 + j];
+              } else {
+                y = (y + a.posx_rows[(size_t)pxy[0] * a.N + n0 + j]) + a.posy_rows[(size_t)pxy[1] * a.N + n0 + j];
+              }
+              v[j] = y;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          }
+        }
+      } else if (EPI == EPI_GELU_GATE || EPI == EPI_GLU) {
+        // Tile columns [0, BN/2) carry the first operand (gate / GLU value),
+        // [BN/2, BN) the second (up / GLU gate) for the same output columns.
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          float g[32], u[32];
+          tmem_ld32(tb + c * 32, g);
+          tmem_ld32(tb + BN / 2 + c * 32, u);
+          if (valid) {
+            const int ng = nb * BN + c * 32, nu = nb * BN + BN / 2 + c * 32;
+            const int no = nb * (BN / 2) + c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float gv = srq_f((g[j] * rs) * a.col_scale[ng + j], a.s_out);
+              float uv = srq_f((u[j] * rs) * a.col_scale[nu + j], a.s_out_b);
+              if (EPI == EPI_GELU_GATE) {
+                g[j] = gelu_tanh_f(gv) * uv;  // runVisionMlpActivationCpu
+              } else {
+                g[j] = gv * (1.0f / (1.0f + expf(-uv)));  // runGluActivationCpu
+              }
+            }
+            if (EPI == EPI_GELU_GATE) {
+              store_f16x2_row(a.out_hi + (size_t)row * a.ldh + no, a.out_lo + (size_t)row * a.ldh + no, g, 32);
+            } else {
+              float* dst = a.out_f32 + (size_t)row * a.ldo + no;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
+            }
+          }
+        }
+      } else if (EPI == EPI_SILU) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          tmem_ld32(tb + c * 32, v);
+          if (valid) {
+            const int n0 = nb * BN + c * 32;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float y = srq_f((v[j] * rs) * a.col_scale[n0 + j], a.s_out);
+              v[j] = y / (1.0f + expf(-y));  // runSiluActivationCpu
+            }
+            store_f16x2_row(a.out_hi + (size_t)row * a.ldh + n0, a.out_lo + (size_t)row * a.ldh + n0, v, 32);
+          }
+        }
+      } else if (EPI == EPI_QKV_VISION) {
+        // 64-column head groups: scale (+srq), head RMSNorm, 2-D RoPE (q, k),
+        // scatter to the attention layouts.
+        const int n_tile0 = nb * BN;
+        const int which = n_tile0 / a.proj_width;  // 0 q, 1 k, 2 v
+        const int head0 = (n_tile0 % a.proj_width) / 64;
+        const int img = valid ? row / a.rows_per_image : 0;
+        const int tok = valid ? row % a.rows_per_image : 0;
+        const float so = which == 0 ? a.s_out : (which == 1 ? a.s_out_b : a.s_out_c);
+        const float* nw = which == 0 ? a.qn_w : (which == 1 ? a.kn_w : nullptr);
+#pragma unroll 1
+        for (int hh = 0; hh < BN / 64; ++hh) {
+          float v[64];
+          tmem_ld32(tb + hh * 64, v);
+          tmem_ld32(tb + hh * 64 + 32, v + 32);
+          if (valid) {
+            const int n0 = n_tile0 + hh * 64;
+            float ss = 0.f;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              v[j] = srq_f((v[j] * rs) * a.col_scale[n0 + j], so);
+              ss = fmaf(v[j], v[j], ss);
+            }
+            const float inv = 1.0f / sqrtf(ss / 64.0f + a.eps);
+#pragma unroll
+            for (int j = 0; j < 64; ++j) v[j] = (v[j] * inv) * (nw ? nw[j] : 1.0f);
+            const int head = head0 + hh;
+            const size_t bh = (size_t)img * a.heads + head;
+            if (which < 2) {
+              const float2* cs = reinterpret_cast<const float2*>(a.rope_cs) + (size_t)tok * 32;
+              float o[64];
+#pragma unroll
+              for (int p = 0; p < 2; ++p) {
+#pragma unroll
+                for (int f = 0; f < 16; ++f) {
+                  const float2 c2 = cs[p * 16 + f];
+                  const float x1 = v[p * 32 + f], x2 = v[p * 32 + 16 + f];
+                  o[p * 32 + f] = x1 * c2.x - x2 * c2.y;
+                  o[p * 32 + 16 + f] = x2 * c2.x + x1 * c2.y;
+                }
+              }
+              __half* dh = (which == 0 ? a.q_hi : a.k_hi) + (bh * a.rows_per_image + tok) * 64;
+              __half* dl = (which == 0 ? a.q_lo : a.k_lo) + (bh * a.rows_per_image + tok) * 64;
+              store_f16x2_row(dh, dl, o, 64);
+            } else {
+              __half* dh = a.vt_hi + bh * 64 * (size_t)a.vt_pitch + tok;
+              __half* dl = a.vt_lo + bh * 64 * (size_t)a.vt_pitch + tok;
+#pragma unroll
+              for (int j = 0; j < 64; ++j) {
+                __half h, l;
+                split_f16(v[j], h, l);
+                dh[(size_t)j * a.vt_pitch] = h;
+                dl[(size_t)j * a.vt_pitch] = l;
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_acce[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// fp16 matrix [rows, cols] (row-major), box 64 columns x box_rows rows, 128B swizzle.
+bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || !base || (cols % 64) != 0 || (reinterpret_cast<uintptr_t>(base) % 16) != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool make_tmap_f16_any(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                       uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || !base || (pitch_elems * 2) % 16 != 0 || pitch_elems < cols ||
+      (reinterpret_cast<uintptr_t>(base) % 16) != 0)
+    return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_elems * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+static int g_num_sms(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v > 0 ? v : 148;
+  }
+  return cache[dev];
+}
+
+template <int BN, int TERMS, int EPI>
+static cudaError_t launch_t(const GemmOperands& op, const GemmArgs& args, cudaStream_t st, int max_ctas) {
+  using C = GemmCfg<BN, TERMS>;
+  auto kern = gemm_tc_kernel<BN, TERMS, EPI>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  CUtensorMap mA0, mA1, mB0, mB1;
+  if (!make_tmap_f16(&mA0, op.a_hi, args.M, args.K, BM)) return cudaErrorInvalidValue;
+  if (!make_tmap_f16(&mB0, op.b_hi, args.N, args.K, BN)) return cudaErrorInvalidValue;
+  mA1 = mA0;
+  mB1 = mB0;
+  if (C::NA == 2 && !make_tmap_f16(&mA1, op.a_lo, args.M, args.K, BM)) return cudaErrorInvalidValue;
+  if (C::NB == 2 && !make_tmap_f16(&mB1, op.b_lo, args.N, args.K, BN)) return cudaErrorInvalidValue;
+  const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
+  int grid = std::min(tiles, g_num_sms(dev));
+  if (max_ctas > 0) grid = std::min(grid, max_ctas);
+  if (grid <= 0) return cudaSuccess;
+  kern<<<grid, kGemmThreads, C::SMEM, st>>>(mA0, mA1, mB0, mB1, args);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args, cudaStream_t st,
+                        int max_ctas) {
+  if (args.K % BK != 0 || args.N % bn != 0 || args.M <= 0) return cudaErrorInvalidValue;
+#define G4M_CASE(BN_, T_, E_) \
+  if (bn == BN_ && terms == T_ && epi == E_) return launch_t<BN_, T_, E_>(op, args, st, max_ctas);
+  G4M_CASE(256, 1, EPI_F32)
+  G4M_CASE(256, 2, EPI_F32)
+  G4M_CASE(128, 3, EPI_F32)
+  G4M_CASE(256, 2, EPI_GELU_GATE)
+  G4M_CASE(256, 2, EPI_GLU)
+  G4M_CASE(256, 2, EPI_SILU)
+  G4M_CASE(256, 2, EPI_QKV_VISION)
+  G4M_CASE(256, 2, EPI_PATCH)
+#undef G4M_CASE
+  return cudaErrorInvalidValue;
+}
+
+// ---------------------------------------------------------------------------
+// Operand preparation kernels
+// ---------------------------------------------------------------------------
+
+// x f32 [rows, cols] -> hi/lo fp16 planes.  s_in > 0 quantises first
+// (srqScalar) and stores the integer code k (exact in fp16, lo = 0); the
+// GEMM epilogue then scales by s_in.  row_scale (optional, [rows]) multiplies
+// x first (the embedder's inverse RMS).
+__global__ void prep_a_kernel(const float* __restrict__ x, long rows, int cols, float s_in, const float* row_scale,
+                              __half* __restrict__ hi, __half* __restrict__ lo) {
+  const long n = rows * (long)cols;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    float v = x[i];
+    if (row_scale) v = v * row_scale[i / cols];
+    __half h, l;
+    if (s_in != 0.0f) {
+      float r = js_round_f(__fdiv_rn(v, s_in));
+      r = fminf(fmaxf(r, -128.0f), 127.0f);
+      h = __float2half_rn(r);
+      l = __float2half_rn(0.0f);
+    } else {
+      split_f16(v, h, l);
+    }
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+cudaError_t prep_a(const float* x, long rows, int cols, float s_in, const float* row_scale, __half* hi, __half* lo,
+                   cudaStream_t st) {
+  const long n = rows * (long)cols;
+  int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
+  if (grid <= 0) return cudaSuccess;
+  prep_a_kernel<<<grid, 256, 0, st>>>(x, rows, cols, s_in, row_scale, hi, lo);
+  return cudaGetLastError();
+}
+
+// Weight conversion to fp16 rows.  dst_row = map ? map[r] : r.
+//   kind 0: int8 [rows, cols]                      value = w
+//   kind 1: unsigned codes packed `bits` per lane   value = code - 2^(bits-1)
+//   kind 2: f32 -> hi (and lo if lo != nullptr)
+//   kind 3: bf16 bits -> fp16
+__global__ void prep_w_kernel(const void* __restrict__ src, int kind, int bits, int rows, int cols, const int* map,
+                              __half* __restrict__ hi, __half* __restrict__ lo) {
+  const long n = (long)rows * cols;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    const long dst = (long)(map ? map[r] : r) * cols + c;
+    float v;
+    if (kind == 0) {
+      v = (float)reinterpret_cast<const int8_t*>(src)[i];
+    } else if (kind == 1) {
+      const uint8_t* w = reinterpret_cast<const uint8_t*>(src);
+      const int vpb = 8 / bits;
+      const long bpr = (long)cols * bits / 8;
+      const uint8_t byte = w[(long)r * bpr + c / vpb];
+      const int code = (byte >> ((c % vpb) * bits)) & ((1 << bits) - 1);
+      v = (float)(code - (1 << (bits - 1)));
+    } else if (kind == 2) {
+      v = reinterpret_cast<const float*>(src)[i];
+    } else {
+      const uint16_t b = reinterpret_cast<const uint16_t*>(src)[i];
+      v = __uint_as_float((uint32_t)b << 16);
+    }
+    if (kind == 2 && lo) {
+      __half h, l;
+      split_f16(v, h, l);
+      hi[dst] = h;
+      lo[dst] = l;
+    } else {
+      hi[dst] = __float2half_rn(v);
+    }
+  }
+}
+
+cudaError_t prep_w(const void* src, int kind, int bits, int rows, int cols, const int* map, __half* hi, __half* lo,
+                   cudaStream_t st) {
+  const long n = (long)rows * cols;
+  int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
+  if (grid <= 0) return cudaSuccess;
+  prep_w_kernel<<<grid, 256, 0, st>>>(src, kind, bits, rows, cols, map, hi, lo);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Exact-semantics SIMT QAT linear for shapes the tensor-core tiles do not
+// cover (in % 64 != 0 or out % 256 != 0).  One thread per output, f32
+// accumulation in the reference's order with every product and sum rounded
+// to f32 (Math.fround), as runQatI8LinearCpu / runPackedQatLinearCpu do
+// (src/kernels/qat.ts:458-487, 215-247).
+// ---------------------------------------------------------------------------
+__global__ void qat_simt_kernel(const float* __restrict__ x, const void* __restrict__ w, int bits,
+                                const float* __restrict__ scale, const float* __restrict__ bias, int rows, int in,
+                                int out, float s_in, float s_out, float* __restrict__ y) {
+  const long total = (long)rows * out;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / out), o = (int)(i % out);
+    const float* xr = x + (long)r * in;
+    float res;
+    if (bits == 0) {
+      const int8_t* wr = reinterpret_cast<const int8_t*>(w) + (long)o * in;
+      float sum = 0.f;
+      for (int c = 0; c < in; ++c) sum = __fadd_rn(sum, __fmul_rn(srq_f(xr[c], s_in), (float)wr[c]));
+      res = srq_f(__fmul_rn(sum, scale[o]), s_out);
+    } else {
+      const uint8_t* wr = reinterpret_cast<const uint8_t*>(w) + (long)o * in * bits / 8;
+      const int vpb = 8 / bits, mask = (1 << bits) - 1;
+      float sqa = 0.f, sa = 0.f;
+      for (int c = 0; c < in; ++c) {
+        const float act = srq_f(xr[c], s_in);
+        const int code = (wr[c / vpb] >> ((c % vpb) * bits)) & mask;
+        sqa = __fadd_rn(sqa, __fmul_rn((float)code, act));
+        sa = __fadd_rn(sa, act);
+      }
+      const float zp = (float)(1 << (bits - 1));
+      res = srq_f(__fmul_rn(scale[o], __fsub_rn(sqa, __fmul_rn(zp, sa))), s_out);
+    }
+    if (bias) res = __fadd_rn(res, bias[o]);
+    y[i] = res;
+  }
+}
+
+cudaError_t qat_linear_simt(const float* x, const void* w, int bits, const float* scale, const float* bias, int rows,
+                            int in, int out, float s_in, float s_out, float* y, cudaStream_t st) {
+  const long total = (long)rows * out;
+  if (total <= 0) return cudaSuccess;
+  const int grid = (int)std::min<long>((total + 127) / 128, 148L * 32);
+  qat_simt_kernel<<<grid, 128, 0, st>>>(x, w, bits, scale, bias, rows, in, out, s_in, s_out, y);
+  return cudaGetLastError();
+}
+
+}  // namespace g4m

@@ -1,0 +1,203 @@
+// Fused row kernels: RMSNorm / residual / scaled residual chains of the
+// vision and audio layers, one warp per row, float4 loads, warp-shuffle
+// reductions, writing both the f32 residual stream and the fp16 hi/lo
+// operand of the next GEMM in the same pass.
+//
+// Replaces runVisionRmsNormWebGpu (src/vision/kernels.ts:161-281, one thread
+// per row there), runResidualAddWebGpu (283-387) and
+// runScaledResidualAddWebGpu (src/audio/kernels.ts:1127-1240), in the orders
+// used by src/vision/encoder.ts:228-297 and src/audio/encoder.ts:761-921.
+#include "g4m_kernels.h"
+#include "g4m_sm100.cuh"
+
+namespace g4m {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float js_round_r(float x) {
+  float f = floorf(x);
+  return (x - f >= 0.5f) ? f + 1.0f : f;
+}
+
+template <int V>
+__device__ __forceinline__ float inv_rms(const float4 (&x)[V], int d, float eps) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) ss += x[i].x * x[i].x + x[i].y * x[i].y + x[i].z * x[i].z + x[i].w * x[i].w;
+  ss = warp_sum(ss);
+  return 1.0f / sqrtf(ss / (float)d + eps);
+}
+
+template <int V>
+__global__ void __launch_bounds__(256) fused_rows_kernel(RowArgs r) {
+  const int lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= r.rows) return;
+  const int d = r.d;
+  float4 h[V];
+  if (r.y) {
+    const float4* y = reinterpret_cast<const float4*>(r.y + row * d);
+#pragma unroll
+    for (int i = 0; i < V; ++i) h[i] = y[lane + 32 * i];
+    if (r.w_post) {
+      const float inv = inv_rms<V>(h, d, r.eps);
+      const float4* w = reinterpret_cast<const float4*>(r.w_post);
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float4 wv = w[lane + 32 * i];
+        h[i] = make_float4((h[i].x * inv) * wv.x, (h[i].y * inv) * wv.y, (h[i].z * inv) * wv.z, (h[i].w * inv) * wv.w);
+      }
+    }
+    if (r.h_in) {
+      const float4* hi = reinterpret_cast<const float4*>(r.h_in + row * d);
+      const float s = r.res_scale;
+#pragma unroll
+      for (int i = 0; i < V; ++i) {
+        const float4 b = hi[lane + 32 * i];
+        h[i] = make_float4(b.x + h[i].x * s, b.y + h[i].y * s, b.z + h[i].z * s, b.w + h[i].w * s);
+      }
+    }
+  } else {
+    const float4* hi = reinterpret_cast<const float4*>(r.h_in + row * d);
+#pragma unroll
+    for (int i = 0; i < V; ++i) h[i] = hi[lane + 32 * i];
+  }
+  if (r.w_out) {
+    const float inv = inv_rms<V>(h, d, r.eps);
+    const float4* w = reinterpret_cast<const float4*>(r.w_out);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 wv = w[lane + 32 * i];
+      h[i] = make_float4((h[i].x * inv) * wv.x, (h[i].y * inv) * wv.y, (h[i].z * inv) * wv.z, (h[i].w * inv) * wv.w);
+    }
+  }
+  if (r.h_out) {
+    float4* ho = reinterpret_cast<float4*>(r.h_out + row * d);
+#pragma unroll
+    for (int i = 0; i < V; ++i) ho[lane + 32 * i] = h[i];
+  }
+  if (r.w_next) {
+    const float inv = inv_rms<V>(h, d, r.eps);
+    const float4* w = reinterpret_cast<const float4*>(r.w_next);
+    __half* ah = r.a_hi + row * r.lda;
+    __half* al = r.a_lo + row * r.lda;
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 wv = w[lane + 32 * i];
+      float v[4] = {(h[i].x * inv) * wv.x, (h[i].y * inv) * wv.y, (h[i].z * inv) * wv.z, (h[i].w * inv) * wv.w};
+      __align__(8) __half hh[4], ll[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (r.s_in_next != 0.0f) {
+          float q = js_round_r(__fdiv_rn(v[u], r.s_in_next));
+          q = fminf(fmaxf(q, -128.0f), 127.0f);
+          hh[u] = __float2half_rn(q);
+          ll[u] = __float2half_rn(0.0f);
+        } else {
+          split_f16(v[u], hh[u], ll[u]);
+        }
+      }
+      const int c = 4 * (lane + 32 * i);
+      *reinterpret_cast<uint2*>(ah + c) = *reinterpret_cast<uint2*>(hh);
+      *reinterpret_cast<uint2*>(al + c) = *reinterpret_cast<uint2*>(ll);
+    }
+  }
+}
+
+cudaError_t fused_rows(const RowArgs& r, cudaStream_t st) {
+  if (r.rows <= 0) return cudaSuccess;
+  const int blocks = (int)((r.rows + 7) / 8);
+  switch (r.d) {
+    case 768:
+      fused_rows_kernel<6><<<blocks, 256, 0, st>>>(r);
+      break;
+    case 1024:
+      fused_rows_kernel<8><<<blocks, 256, 0, st>>>(r);
+      break;
+    case 1536:
+      fused_rows_kernel<12><<<blocks, 256, 0, st>>>(r);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+// Per-row inverse RMS (weightless) folded into an fp16 hi/lo operand: the
+// embedder's normalisation (src/embedder/index.ts:126-140).
+template <int V>
+__global__ void __launch_bounds__(256) inv_rms_operand_kernel(const float* x, long rows, int d, float eps, __half* hi,
+                                                              __half* lo) {
+  const int lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  float4 h[V];
+  const float4* src = reinterpret_cast<const float4*>(x + row * d);
+#pragma unroll
+  for (int i = 0; i < V; ++i) h[i] = src[lane + 32 * i];
+  const float inv = inv_rms<V>(h, d, eps);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    float v[4] = {h[i].x * inv, h[i].y * inv, h[i].z * inv, h[i].w * inv};
+    __align__(8) __half hh[4], ll[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) split_f16(v[u], hh[u], ll[u]);
+    const int c = 4 * (lane + 32 * i);
+    *reinterpret_cast<uint2*>(hi + row * d + c) = *reinterpret_cast<uint2*>(hh);
+    *reinterpret_cast<uint2*>(lo + row * d + c) = *reinterpret_cast<uint2*>(ll);
+  }
+}
+
+cudaError_t row_inv_rms_operand(const float* x, long rows, int d, float eps, __half* hi, __half* lo, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const int blocks = (int)((rows + 7) / 8);
+  switch (d) {
+    case 768:
+      inv_rms_operand_kernel<6><<<blocks, 256, 0, st>>>(x, rows, d, eps, hi, lo);
+      break;
+    case 1024:
+      inv_rms_operand_kernel<8><<<blocks, 256, 0, st>>>(x, rows, d, eps, hi, lo);
+      break;
+    case 1536:
+      inv_rms_operand_kernel<12><<<blocks, 256, 0, st>>>(x, rows, d, eps, hi, lo);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+__global__ void add_bias_rows_kernel(float* y, const float* b, long n, int d) {
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    y[i] = y[i] + b[i % d];
+}
+
+cudaError_t add_bias_rows(float* y, const float* b, long rows, int d, cudaStream_t st) {
+  const long n = rows * d;
+  if (n <= 0) return cudaSuccess;
+  const int grid = (int)((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  add_bias_rows_kernel<<<grid, 256, 0, st>>>(y, b, n, d);
+  return cudaGetLastError();
+}
+
+__global__ void gather_rows_kernel(const float* src, const int* idx, long n, int d, float* dst) {
+  const long total = n * d;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long r = i / d;
+    dst[i] = src[(long)idx[r] * d + (i % d)];
+  }
+}
+
+cudaError_t gather_rows(const float* src, const int* rows_idx, long n, int d, float* dst, cudaStream_t st) {
+  const long total = n * d;
+  if (total <= 0) return cudaSuccess;
+  const int grid = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+  gather_rows_kernel<<<grid, 256, 0, st>>>(src, rows_idx, n, d, dst);
+  return cudaGetLastError();
+}
+
+}  // namespace g4m

@@ -1,0 +1,194 @@
+// Vision tower helper kernels: patch operand, 3x3 pooler fused with the
+// embedder's inverse RMS, and an fp32 SIMT flash attention (the exact
+// baseline the tcgen05 attention is checked against on the device).
+#include "g4m_kernels.h"
+#include "g4m_sm100.cuh"
+
+namespace g4m {
+
+// Patchify (src/preprocess/image.ts:133-148) + the 2*(p - 0.5) scaling of
+// runVisionPatchEmbeddingCpu (src/vision/kernels.ts:1008-1012), written as
+// the fp16 hi/lo operand of the patch-projection GEMM.  pixels are
+// [n_images][height][width][3] float32; rows are (image, patch_y, patch_x),
+// columns (dy * patch + dx) * 3 + channel.
+__global__ void patch_operand_kernel(const float* __restrict__ px, int n_images, int height, int width, int patch,
+                                     __half* __restrict__ hi, __half* __restrict__ lo) {
+  const int gw = width / patch, gh = height / patch;
+  const int pp = patch * patch * 3;
+  const long total = (long)n_images * gh * gw * pp;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / pp;
+    const int col = (int)(i % pp);
+    const int img = (int)(row / ((long)gh * gw));
+    const int p = (int)(row % ((long)gh * gw));
+    const int py = p / gw, pxx = p % gw;
+    const int c = col % 3, dx = (col / 3) % patch, dy = col / (3 * patch);
+    const float v = px[(((long)img * height + py * patch + dy) * width + pxx * patch + dx) * 3 + c];
+    const double s = 2.0 * ((double)v - 0.5);
+    const __half h = __double2half(s);
+    hi[i] = h;
+    lo[i] = __double2half(s - (double)__half2float(h));
+  }
+}
+
+cudaError_t vision_patch_operand(const float* pixels, int n_images, int height, int width, int patch, __half* hi,
+                                 __half* lo, cudaStream_t st) {
+  const long total = (long)n_images * (height / patch) * (width / patch) * patch * patch * 3;
+  if (total <= 0) return cudaSuccess;
+  const int grid = (int)((total + 255) / 256 < 148 * 32 ? (total + 255) / 256 : 148 * 32);
+  patch_operand_kernel<<<grid, 256, 0, st>>>(pixels, n_images, height, width, patch, hi, lo);
+  return cudaGetLastError();
+}
+
+// runVisionPoolerCpu (src/vision/kernels.ts:815-833) followed by the
+// embedder's weightless RMSNorm (src/embedder/index.ts:126-140): one warp
+// per soft token, d = 768.
+__global__ void __launch_bounds__(256) pool_operand_kernel(const float* __restrict__ h, const int* __restrict__ idx,
+                                                           int n_images, int rows_per_image, int tokens, int k2,
+                                                           float eps, float* pooled_out, __half* hi, __half* lo) {
+  constexpr int D = 768, V = D / 128;
+  const int lane = threadIdx.x & 31;
+  const long w = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (w >= (long)n_images * tokens) return;
+  const int img = (int)(w / tokens), t = (int)(w % tokens);
+  float4 acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < k2; ++j) {
+    const int p = idx[t * k2 + j];
+    if (p < 0) continue;
+    const float4* src = reinterpret_cast<const float4*>(h + ((long)img * rows_per_image + p) * D);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const float4 v = src[lane + 32 * i];
+      acc[i].x += v.x;
+      acc[i].y += v.y;
+      acc[i].z += v.z;
+      acc[i].w += v.w;
+    }
+  }
+  const float scale = sqrtf((float)D) / (float)k2;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    acc[i] = make_float4(acc[i].x * scale, acc[i].y * scale, acc[i].z * scale, acc[i].w * scale);
+    ss += acc[i].x * acc[i].x + acc[i].y * acc[i].y + acc[i].z * acc[i].z + acc[i].w * acc[i].w;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+  const long orow = (long)img * tokens + t;
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const int c = 4 * (lane + 32 * i);
+    if (pooled_out) *reinterpret_cast<float4*>(pooled_out + orow * D + c) = acc[i];
+    float v[4] = {acc[i].x * inv, acc[i].y * inv, acc[i].z * inv, acc[i].w * inv};
+    __align__(8) __half hh[4], ll[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) split_f16(v[u], hh[u], ll[u]);
+    *reinterpret_cast<uint2*>(hi + orow * D + c) = *reinterpret_cast<uint2*>(hh);
+    *reinterpret_cast<uint2*>(lo + orow * D + c) = *reinterpret_cast<uint2*>(ll);
+  }
+}
+
+cudaError_t vision_pool_operand(const float* h, const int* pool_idx, int n_images, int rows_per_image, int tokens,
+                                int k2, int d, float eps, float* pooled_out, __half* hi, __half* lo, cudaStream_t st) {
+  if (d != 768) return cudaErrorInvalidValue;
+  const long warps = (long)n_images * tokens;
+  if (warps <= 0) return cudaSuccess;
+  pool_operand_kernel<<<(int)((warps + 7) / 8), 256, 0, st>>>(h, pool_idx, n_images, rows_per_image, tokens, k2, eps,
+                                                               pooled_out, hi, lo);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// fp32 SIMT flash attention, head_dim 64, scale 1, no mask
+// (runVisionAttentionBodyCpu, src/vision/kernels.ts:75-131).
+// One thread per query row, 128 queries per CTA, 64-key tiles in smem.
+// Output: o[(img * n + tok)][head * 64 + d] as fp16 hi/lo.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) attn_simt_kernel(const __half* __restrict__ qh, const __half* __restrict__ ql,
+                                                        const __half* __restrict__ kh, const __half* __restrict__ kl,
+                                                        const __half* __restrict__ vth,
+                                                        const __half* __restrict__ vtl, int n, int vt_pitch,
+                                                        int heads, __half* __restrict__ oh,
+                                                        __half* __restrict__ ol) {
+  __shared__ float Ks[64][65];
+  __shared__ float Vs[64][65];
+  const int bh = blockIdx.y;
+  const int qrow = blockIdx.x * 128 + threadIdx.x;
+  const bool valid = qrow < n;
+  float q[64], o[64];
+  const size_t qbase = ((size_t)bh * n + (valid ? qrow : 0)) * 64;
+#pragma unroll
+  for (int d = 0; d < 64; ++d) {
+    q[d] = __half2float(qh[qbase + d]) + __half2float(ql[qbase + d]);
+    o[d] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  for (int k0 = 0; k0 < n; k0 += 64) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * 64; i += 128) {
+      const int kr = i / 64, d = i % 64;
+      const int key = k0 + kr;
+      float kv = 0.f, vv = 0.f;
+      if (key < n) {
+        const size_t ki = ((size_t)bh * n + key) * 64 + d;
+        kv = __half2float(kh[ki]) + __half2float(kl[ki]);
+        const size_t vi = ((size_t)bh * 64 + d) * vt_pitch + key;
+        vv = __half2float(vth[vi]) + __half2float(vtl[vi]);
+      }
+      Ks[kr][d] = kv;
+      Vs[kr][d] = vv;
+    }
+    __syncthreads();
+    const int kn = min(64, n - k0);
+    float s[64];
+    float mt = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      float acc = 0.f;
+#pragma unroll
+      for (int d = 0; d < 64; ++d) acc = fmaf(q[d], Ks[j][d], acc);
+      s[j] = j < kn ? acc : -INFINITY;
+      mt = fmaxf(mt, s[j]);
+    }
+    const float mn = fmaxf(m, mt);
+    const float corr = expf(m - mn);
+    l *= corr;
+#pragma unroll
+    for (int d = 0; d < 64; ++d) o[d] *= corr;
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+      const float p = expf(s[j] - mn);
+      l += p;
+#pragma unroll
+      for (int d = 0; d < 64; ++d) o[d] = fmaf(p, Vs[j][d], o[d]);
+    }
+    m = mn;
+  }
+  if (!valid) return;
+  const int img = bh / heads, head = bh % heads;
+  const size_t orow = (size_t)img * n + qrow;
+  const float inv = 1.0f / l;
+  __half* dh = oh + orow * (size_t)(heads * 64) + head * 64;
+  __half* dl = ol + orow * (size_t)(heads * 64) + head * 64;
+#pragma unroll
+  for (int d = 0; d < 64; ++d) {
+    __half h, lo;
+    split_f16(o[d] * inv, h, lo);
+    dh[d] = h;
+    dl[d] = lo;
+  }
+}
+
+cudaError_t vision_attention_simt(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
+                                  const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
+                                  __half* o_hi, __half* o_lo, cudaStream_t st) {
+  if (bh <= 0 || n <= 0) return cudaSuccess;
+  dim3 grid((n + 127) / 128, bh);
+  attn_simt_kernel<<<grid, 128, 0, st>>>(q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo, n, vt_pitch, heads, o_hi, o_lo);
+  return cudaGetLastError();
+}
+
+}  // namespace g4m
