@@ -60,9 +60,11 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, uuid: str):
-        self.uuid = uuid
+    def __init__(self, uuid: str, index: int):
+        self.uuid = uuid.lower().replace("gpu-", "")
+        self.index = index
         self.rows = []
+        self.all = []
         self.proc = None
 
     def start(self):
@@ -76,8 +78,10 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9 and self.uuid and self.uuid in parts[0]:
-                self.rows.append(parts)
+            if len(parts) >= 9:
+                self.all.append(parts)
+                if self.uuid and self.uuid in parts[0].lower():
+                    self.rows.append(parts)
 
     def stop(self):
         if self.proc:
@@ -86,6 +90,10 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+        if not self.rows and self.all:  # UUID formats differ: fall back to the device ordinal
+            uuids = sorted({r[0] for r in self.all})
+            pick = uuids[self.index] if self.index < len(uuids) else uuids[0]
+            self.rows = [r for r in self.all if r[0] == pick]
         sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
         mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -141,6 +149,53 @@ def cpu_vision_sample(threads: int):
     return per_image, "1 image 768x768: patch embed + 1 of 16 encoder layers (x16) + pooler/embedder"
 
 
+AUDIO_D, AUDIO_FF, AUDIO_OUT = 1024, 4096, 1536
+
+
+def audio_kernel_flops(M: int):
+    """Algorithmic FLOPs per launch of the audio GEMMs over M packed rows."""
+    return {
+        "gemm_ffw1": 2.0 * M * AUDIO_FF * AUDIO_D,
+        "gemm_ffw2": 2.0 * M * AUDIO_D * AUDIO_FF,
+        "gemm_qkv": 2.0 * M * 3 * AUDIO_D * AUDIO_D,
+        "gemm_post": 2.0 * M * AUDIO_D * AUDIO_D,
+        "gemm_lconv_start": 2.0 * M * 2 * AUDIO_D * AUDIO_D,
+        "gemm_lconv_end": 2.0 * M * AUDIO_D * AUDIO_D,
+        "gemm_in_proj": 2.0 * M * AUDIO_D * AUDIO_D,
+        "gemm_out_proj": 2.0 * M * AUDIO_OUT * AUDIO_D,
+        "gemm_embed": 2.0 * M * 1536 * AUDIO_OUT,
+    }
+
+
+def audio_rows(n: int) -> int:
+    f = (160 + n - 321) // 160 + 1 if 160 + n >= 321 else 0
+    t0 = (f - 1) // 2 + 1 if f else 0
+    return (t0 - 1) // 2 + 1 if f else 0
+
+
+def cpu_audio_sample(threads: int):
+    """Oracle on one 10 s clip (cfg2): log-mel + subsample + one of 12
+    conformer layers (x12) + output projection / embedder.  Returns (seconds
+    of compute per second of audio, description)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    syn = importlib.import_module(PKG + ".synthetic")
+    O.set_threads(threads)
+    W = syn.audio_weights(0, layers=1)
+    x = syn.audio_samples(0, 160000)
+    t0 = time.perf_counter()
+    pre = O.preprocess_audio(x, pad_to_multiple_of=None)
+    h, mask = O.audio_subsample(W, pre["inputFeatures"], pre["inputFeaturesMask"])
+    t1 = time.perf_counter()
+    h = O.audio_layer(W, 0, h)
+    t2 = time.perf_counter()
+    proj = O.add_bias_rows(O.f32_linear_rows(h, W["model.audio_tower.output_proj.weight"]), W["model.audio_tower.output_proj.bias"])
+    O.embedder(proj, W["model.embed_audio.embedding_projection.weight"])
+    t3 = time.perf_counter()
+    secs = (t1 - t0) + 12 * (t2 - t1) + (t3 - t2)
+    return secs / 10.0, "one 10 s clip (250 rows): log-mel + subsample + 1 of 12 conformer layers (x12) + output/embedder"
+
+
 def run_reference(args):
     rank = env_int("RANK", 0)
     if rank != 0:
@@ -164,7 +219,97 @@ def run_reference(args):
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
+    if not args.no_audio:
+        a_secs = [cpu_audio_sample(threads)[0] for _ in range(max(1, min(args.steps, 3)))]
+        av = len(a_secs) / sum(a_secs)
+        line["audio"] = {"metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": av,
+                         "unit": "audio-s/s", "cpu_baseline": {"value": av, "unit": "audio-s/s", "cores": threads,
+                                                               "kind": "port", "sample": cpu_audio_sample.__doc__.split(".")[0]}}
     print(json.dumps(line), flush=True)
+
+
+def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
+    """Batched audio (cfg4): 128 clips per GPU, lengths U[1, 30] s, packed
+    without padding rows.  Returns the sub-object of the JSON line (rank 0)."""
+    import numpy as np
+    import torch
+    d = os.path.join(os.environ.get("TMPDIR", "/tmp"), "g4m_bench")
+    p = os.path.join(d, "audio12_seed0.safetensors")
+    if rank == 0 and not os.path.exists(p):
+        tmp = p + f".tmp{os.getpid()}"
+        syn.write_safetensors(tmp, syn.audio_weights(0, layers=12))
+        os.replace(tmp, p)
+    barrier()
+    ctx = ctx_cls([torch.cuda.current_device()])
+    ctx.load_weights(p)
+    n = args.clips
+    lens = syn.audio_batch_lengths(1000 + rank, n)
+    total = int(lens.sum())
+    host = torch.empty(total, dtype=torch.float32).pin_memory()
+    offs = np.zeros(n, np.int64)
+    o = 0
+    for i, L in enumerate(lens):
+        host[o:o + int(L)] = torch.from_numpy(syn.audio_samples(5000 + rank * n + i, int(L)))
+        offs[i] = o
+        o += int(L)
+    dev = host.cuda()
+    rows = sum(audio_rows(int(L)) for L in lens)
+    out = torch.empty((rows, 1536), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    step = lambda: ctx.audio_embed_device(dev.data_ptr(), offs, lens, out.data_ptr(), stream=stream.cuda_stream)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    e1.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    audio_seconds = float(lens.sum()) / 16000.0
+    value = world * audio_seconds * args.steps / (ms / 1000.0)
+    ctx.profile_begin()
+    step()
+    prof = ctx.profile_end()
+    flops = audio_kernel_flops(rows)
+    gem = {k: v for k, v in prof.items() if k in flops}
+    dom = max(gem, key=lambda k: gem[k][1])
+    peak = measured_peaks().get("bf16_tflops_sustained") or 1400.0
+    ach = flops[dom] / (gem[dom][1] / gem[dom][0] / 1000.0) / 1e12
+    # end to end with pinned host clips through the C ABI batch call
+    clips = [host[int(offs[i]):int(offs[i]) + int(lens[i])].numpy() for i in range(n)]
+    ctx.audio_embed(clips, 16000, 12)
+    barrier()
+    k_e2e = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(k_e2e):
+        ctx.audio_embed(clips, 16000, 12)
+    te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    res = {
+        "metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": value, "unit": "audio-s/s",
+        "ms_per_step": ms / args.steps,
+        "config": {"workload": f"batched audio: {n} clips/GPU, lengths U[1,30] s (seeded), packed rows (no padding)",
+                   "clips_per_gpu": n, "audio_seconds_per_gpu": audio_seconds, "encoder_rows_per_gpu": rows},
+        "e2e": {"value": world * audio_seconds * k_e2e / float(te.item()), "unit": "audio-s/s",
+                "h2d_bytes_per_step": total * 4, "d2h_bytes_per_step": rows * 1536 * 4},
+        "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+                     "frac": ach / peak, "peak_source": "measured (bf16 cuBLAS, sustained)", "traffic": None,
+                     "launch_ms": gem[dom][1] / gem[dom][0], "flop_per_launch": flops[dom]},
+        "kernel_ms_per_step": {k: round(v[1], 4) for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        spa, desc = cpu_audio_sample(os.cpu_count() or 1)
+        res["cpu_baseline"] = {"value": 1.0 / spa, "unit": "audio-s/s", "cores": os.cpu_count() or 1, "kind": "port",
+                               "sample": desc}
+    ctx.close()
+    return res
 
 
 def run_ours(args):
@@ -197,17 +342,17 @@ def run_ours(args):
         pix_host[i] = torch.from_numpy(syn.image_pixels(rank * B + i, H, Wd))
     pix = pix_host.cuda()
     out = torch.empty((B * tokens, TEXT), dtype=torch.float32, device="cuda")
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()  # a real stream: the library launches on it, the events bracket it
 
     def step():
         ctx.vision_embed_device(pix.data_ptr(), B, H, Wd, out.data_ptr(), max_soft, layers, stream.cuda_stream)
 
-    for _ in range(args.warmup):
-        step()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
     torch.cuda.synchronize()
     barrier()
-    uuid = str(torch.cuda.get_device_properties(local).uuid)
-    clocks = ClockSampler(uuid)
+    clocks = ClockSampler(str(torch.cuda.get_device_properties(local).uuid), local)
     clocks.start()
     launches0 = native.kernel_launches()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -275,6 +420,12 @@ def run_ours(args):
         s, desc = cpu_vision_sample(threads)
         cpu = {"value": 1.0 / s, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc}
 
+    launches_total = launches
+    audio = None
+    if not args.no_audio:
+        ctx.close()
+        audio = run_audio(args, native.Context, native, syn, rank, world, dist, barrier)
+
     if rank == 0:
         line = {
             "impl": "g4m", "metric": "images/s (vision tower 768x768, 16 layers, + embedder)", "value": value,
@@ -293,8 +444,11 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "clocks": clk,
         }
+        if audio:
+            line["audio"] = audio
         print(json.dumps(line), flush=True)
-    ctx.close()
+    if args.no_audio:
+        ctx.close()
     if dist:
         dist.destroy_process_group()
 
@@ -307,6 +461,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--batch", type=int, default=64, help="images per GPU per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-audio", action="store_true", help="skip the batched-audio half of the metric")
+    ap.add_argument("--clips", type=int, default=128, help="audio clips per GPU per step")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

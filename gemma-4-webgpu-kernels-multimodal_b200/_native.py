@@ -42,6 +42,8 @@ _SIGS = [
     ("g4m_vision_layers", _I, [_VP, _I, _I, _I, _I, _I, _I, _VP]),
     ("g4m_audio_embed_batch", _I, [_VP, _I, _VP, _VP, _I, _I, _I64, _VP, _VP, _VP]),
     ("g4m_audio_embed_device", _I, [_VP, _I, _I, _VP, _VP, _VP, _I, _I, _I64, _VP, _VP, _VP]),
+    ("g4m_audio_debug_hidden", _I, [_VP, _I, _I, _VP, ctypes.c_size_t]),
+    ("g4m_audio_layers", _I, [_VP, _I, _I, _VP, _I, _I, _VP]),
     ("g4m_image_token_layout", _I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I64)]),
     ("g4m_audio_soft_token_count", _I64, [_I64, _I, _I, _I]),
     ("g4m_checksum_floats", ctypes.c_double, [_VP, _I64]),
@@ -217,6 +219,17 @@ class Context:
         check(lib().g4m_audio_embed_batch(self.h, n, ctypes.cast(pin, ctypes.c_void_p), ptr(lens), sampling_rate, layer_count,
                                           int(max_samples), ctypes.cast(pout, ctypes.c_void_p), ptr(rows), ptr(status)))
         return [o[: int(r)] for o, r in zip(outs, rows)], rows
+
+    def audio_debug_hidden(self, rows: int, which: int = 1, device=0) -> np.ndarray:
+        out = np.empty((rows, 1024), np.float32)
+        check(lib().g4m_audio_debug_hidden(self.h, device, which, ptr(out), out.size))
+        return out
+
+    def audio_layers(self, h: np.ndarray, rows_per_clip, first: int, count: int, device=0) -> np.ndarray:
+        h = np.ascontiguousarray(h, dtype=np.float32).copy()
+        rows = np.ascontiguousarray(rows_per_clip, dtype=np.int32)
+        check(lib().g4m_audio_layers(self.h, device, rows.size, ptr(rows), first, count, ptr(h)))
+        return h
 
     def audio_embed_device(self, samples_ptr: int, offsets: np.ndarray, lengths: np.ndarray, out_ptr: int,
                            sampling_rate=16000, layer_count=12, max_samples=0, stream: int = 0, device=0) -> np.ndarray:

@@ -13,8 +13,10 @@
 //   warp 0      TMA: Q once, then K / V^T tiles of 128 keys (2-stage ring)
 //   warp 1      TMEM owner + MMA issuer: S into two TMEM buffers (S_{j+1}
 //               overlaps the softmax of S_j), P*V into a third region
-//   warps 2..5  softmax, one query row per thread: online max / sum, P in
-//               128-byte-swizzled smem for the next MMA, O kept in registers
+//   warps 2..9  softmax: warpgroup g runs an independent online softmax over
+//               key columns [64g, 64g + 64) of every S tile (its own max, sum,
+//               P sub-tile, P*V accumulator and O registers); the two partial
+//               results are merged once at the end.  One query row per thread.
 // Layouts: Q, K [bh][n][64]; V^T [bh][64][vt_pitch] (keys >= n read as zero);
 // O [(img*n + q)][head*64 + d].
 #include "g4m_kernels.h"
@@ -24,7 +26,8 @@ namespace g4m {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kSoftGroups = 2;                        // softmax warpgroups (key-column halves)
+constexpr int kThreads = 64 + 128 * kSoftGroups;
 constexpr int QT = 128;                // queries per CTA
 constexpr int KT = 128;                // keys per tile
 constexpr int HD = 64;
@@ -35,8 +38,9 @@ constexpr int KV_STAGE = 4 * TILE_BYTES;
 constexpr int P_OFF = KV_OFF + 2 * KV_STAGE;     // p hi (2 sub-tiles), p lo (2 sub-tiles)
 constexpr int SMEM_BYTES = P_OFF + 4 * TILE_BYTES;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) PV [256,320)
+constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) PV0 [256,320) PV1 [320,384)
 constexpr float kLog2e = 1.4426950408889634f;
+static_assert(SMEM_ALLOC + 512 <= 232448, "dynamic + static shared memory exceeds 227 KB per block");
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -93,9 +97,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&b_kvf[s], 1);
       mbar_init(&b_kve[s], 1);
       mbar_init(&b_sf[s], 1);
-      mbar_init(&b_se[s], 4);
+      mbar_init(&b_se[s], 4 * kSoftGroups);
     }
-    mbar_init(&b_p, 4);
+    mbar_init(&b_p, 4 * kSoftGroups);
     mbar_init(&b_pv, 1);
     fence_mbar_init();
   }
@@ -177,15 +181,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const int s = j & 1;
         const uint32_t vh = smem_u32(sm + KV_OFF + s * KV_STAGE + 2 * TILE_BYTES), vl = vh + TILE_BYTES;
-        const uint32_t d = tmem + 2 * KT;
+        // one K=64 P*V chain per key half, each into its own accumulator
 #pragma unroll
-        for (int kk = 0; kk < KT / 16; ++kk) {
-          const uint32_t sub = (kk >> 2), off = (kk & 3) * 32;
-          const uint64_t dph = desc_k_sw128(ph + sub * TILE_BYTES + off);
-          const uint64_t dvh = desc_k_sw128(vh + sub * (TILE_BYTES / 2) + off);
-          mma_f16_ss(d, dph, dvh, id_pv, kk > 0 ? 1u : 0u);
-          mma_f16_ss(d, dph, desc_k_sw128(vl + sub * (TILE_BYTES / 2) + off), id_pv, 1u);
-          mma_f16_ss(d, desc_k_sw128(pl + sub * TILE_BYTES + off), dvh, id_pv, 1u);
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t d = tmem + 2 * KT + half * HD;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t off = kk * 32;
+            const uint64_t dph = desc_k_sw128(ph + half * TILE_BYTES + off);
+            const uint64_t dvh = desc_k_sw128(vh + half * (TILE_BYTES / 2) + off);
+            mma_f16_ss(d, dph, dvh, id_pv, kk > 0 ? 1u : 0u);
+            mma_f16_ss(d, dph, desc_k_sw128(vl + half * (TILE_BYTES / 2) + off), id_pv, 1u);
+            mma_f16_ss(d, desc_k_sw128(pl + half * TILE_BYTES + off), dvh, id_pv, 1u);
+          }
         }
         mma_commit(&b_pv);
         mma_commit(&b_kve[s]);
@@ -197,12 +205,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // softmax warps
+    // softmax warps: group g = key half g of every tile
     const int q = warp & 3;
+    const int g = (warp - 2) >> 2;
     const int r = 32 * q + lane;
     const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    uint8_t* ph = sm + P_OFF;
-    uint8_t* pl = ph + 2 * TILE_BYTES;
+    constexpr int KH = KT / kSoftGroups;  // 64 keys per group
+    uint8_t* ph = sm + P_OFF + g * TILE_BYTES;  // this group's P sub-tile (hi)
+    uint8_t* pl = ph + 2 * TILE_BYTES;          // (lo)
+    const uint32_t pv_col = 2 * KT + g * HD;    // this group's P*V accumulator
     float o[HD];
 #pragma unroll
     for (int i = 0; i < HD; ++i) o[i] = 0.f;
@@ -213,50 +224,77 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&b_sf[b], k & 1, err, kErrWaitAccFull, &abort_flag));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sr[KT];
-#pragma unroll
-      for (int c = 0; c < KT / 32; ++c) tmem_ld32_nw(tmem + lane_base + b * KT + c * 32, sr + c * 32);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&b_se[b]);
-      float s[KT];
+      const uint32_t sbase = tmem + lane_base + b * KT + g * KH;
+      const int kvalid = n - j * KT - g * KH;  // valid keys among this group's 64
+      const bool full = kvalid >= KH;
+      // pass 1: running max over this group's keys
       float mt = -INFINITY;
-      const int kvalid = n - j * KT;
 #pragma unroll
-      for (int c = 0; c < KT; ++c) {
-        s[c] = c < kvalid ? __uint_as_float(sr[c]) : -INFINITY;
-        mt = fmaxf(mt, s[c]);
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t sr[32];
+        tmem_ld32_nw(sbase + hb * 32, sr);
+        tmem_wait_ld();
+        if (full) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) mt = fmaxf(mt, __uint_as_float(sr[c]));
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c)
+            if (hb * 32 + c < kvalid) mt = fmaxf(mt, __uint_as_float(sr[c]));
+        }
       }
-      const float mn = fmaxf(m, mt);
+      const float mn = fmaxf(m, mt);  // -inf only while this group has seen no valid key
       const float alpha = (m == -INFINITY) ? 0.f : ex2((m - mn) * kLog2e);
-      float rs = 0.f;
-#pragma unroll
-      for (int c = 0; c < KT; ++c) {
-        s[c] = ex2((s[c] - mn) * kLog2e);
-        rs += s[c];
-      }
+      const float mnl = (mn == -INFINITY) ? 0.f : mn * kLog2e;
       if (j > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(&b_pv, (j - 1) & 1, err, kErrWaitAccFull, &abort_flag));
         if (!ok) break;
         tc_fence_after();
-        uint32_t pv[HD];
-        tmem_ld32_nw(tmem + lane_base + 2 * KT, pv);
-        tmem_ld32_nw(tmem + lane_base + 2 * KT + 32, pv + 32);
+        uint32_t pv[32];
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          tmem_ld32_nw(tmem + lane_base + pv_col + hb * 32, pv);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[hb * 32 + i] = fmaf(o[hb * 32 + i], alpha_prev, __uint_as_float(pv[i]));
+        }
+      }
+      // pass 2: probabilities, row sum, P (hi / lo) into this group's swizzled sub-tile
+      float rs = 0.f;
+#pragma unroll
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t sr[32];
+        tmem_ld32_nw(sbase + hb * 32, sr);
         tmem_wait_ld();
+        if (full) {
 #pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(pv[i]));
+          for (int c = 0; c < 32; ++c) {
+            const float p = ex2(fmaf(__uint_as_float(sr[c]), kLog2e, -mnl));
+            sr[c] = __float_as_uint(p);
+            rs += p;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float p = (hb * 32 + c < kvalid) ? ex2(fmaf(__uint_as_float(sr[c]), kLog2e, -mnl)) : 0.f;
+            sr[c] = __float_as_uint(p);
+            rs += p;
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 32; c += 8) {
+          uint32_t hv[4], lv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u)
+            split2_f16(__uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]), hv[u], lv[u]);
+          const uint32_t off = sw128_off(r, hb * 32 + c);
+          *reinterpret_cast<uint4*>(ph + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+          *reinterpret_cast<uint4*>(pl + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        }
       }
-      // P (hi / lo) into two [128 x 64] swizzled sub-tiles per plane
-#pragma unroll
-      for (int c = 0; c < KT; c += 8) {
-        __align__(16) __half hh[8], ll[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) split_f16(s[c + u], hh[u], ll[u]);
-        const uint32_t off = (uint32_t)(c >> 6) * TILE_BYTES + sw128_off(r, c & 63);
-        *reinterpret_cast<uint4*>(ph + off) = *reinterpret_cast<uint4*>(hh);
-        *reinterpret_cast<uint4*>(pl + off) = *reinterpret_cast<uint4*>(ll);
-      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b_se[b]);  // S buffer b may be overwritten (tile j + 2)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -269,27 +307,65 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&b_pv, (T - 1) & 1, err, kErrWaitAccFull, &abort_flag));
       if (ok) {
         tc_fence_after();
-        uint32_t pv[HD];
-        tmem_ld32_nw(tmem + lane_base + 2 * KT, pv);
-        tmem_ld32_nw(tmem + lane_base + 2 * KT + 32, pv + 32);
-        tmem_wait_ld();
+        uint32_t pv[32];
 #pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = fmaf(o[i], alpha_prev, __uint_as_float(pv[i]));
-        const int qrow = q0 + r;
-        if (qrow < n) {
-          const int img = bh / heads, head = bh % heads;
-          const size_t orow = (size_t)img * n + qrow;
-          const float inv = 1.0f / l;
-          __half* dh = o_hi + orow * (size_t)(heads * HD) + head * HD;
-          __half* dl = o_lo + orow * (size_t)(heads * HD) + head * HD;
+        for (int hb = 0; hb < 2; ++hb) {
+          tmem_ld32_nw(tmem + lane_base + pv_col + hb * 32, pv);
+          tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < HD; i += 8) {
-            __align__(16) __half hh[8], ll[8];
+          for (int i = 0; i < 32; ++i) o[hb * 32 + i] = fmaf(o[hb * 32 + i], alpha_prev, __uint_as_float(pv[i]));
+        }
+      }
+    }
+    // Merge the two key halves (flash-decoding style): group g keeps output
+    // columns [32g, 32g + 32) and receives the partner's (m, l, O) for them
+    // through the P region, idle once the last P*V has completed.
+    float* xch = reinterpret_cast<float*>(sm + P_OFF);  // [group][row][34]
+    {
+      float* mine = xch + ((size_t)g * 128 + r) * 34;
+      mine[0] = m;
+      mine[1] = l;
+      if (g == 0) {  // hand the partner the columns it keeps (constant indices)
 #pragma unroll
-            for (int u = 0; u < 8; ++u) split_f16(o[i + u] * inv, hh[u], ll[u]);
-            *reinterpret_cast<uint4*>(dh + i) = *reinterpret_cast<uint4*>(hh);
-            *reinterpret_cast<uint4*>(dl + i) = *reinterpret_cast<uint4*>(ll);
+        for (int i = 0; i < 32; ++i) mine[2 + i] = o[32 + i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mine[2 + i] = o[i];
+      }
+    }
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + q), "r"(32 * kSoftGroups) : "memory");
+    if (ok) {
+      const float* other = xch + ((size_t)(1 - g) * 128 + r) * 34;
+      const float m2 = other[0], l2 = other[1];
+      const float mm = fmaxf(m, m2);
+      const float a1 = (m == -INFINITY) ? 0.f : ex2((m - mm) * kLog2e);
+      const float a2 = (m2 == -INFINITY) ? 0.f : ex2((m2 - mm) * kLog2e);
+      const float inv = 1.0f / (l * a1 + l2 * a2);
+      float own[32];
+      if (g == 0) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) own[i] = o[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) own[i] = o[32 + i];
+      }
+      const int qrow = q0 + r;
+      if (qrow < n) {
+        const int img = bh / heads, head = bh % heads;
+        const size_t orow = (size_t)img * n + qrow;
+        __half* dh = o_hi + orow * (size_t)(heads * HD) + head * HD + 32 * g;
+        __half* dl = o_lo + orow * (size_t)(heads * HD) + head * HD + 32 * g;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+          uint32_t hv[4], lv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float v0 = (own[i + 2 * u] * a1 + other[2 + i + 2 * u] * a2) * inv;
+            const float v1 = (own[i + 2 * u + 1] * a1 + other[2 + i + 2 * u + 1] * a2) * inv;
+            split2_f16(v0, v1, hv[u], lv[u]);
           }
+          *reinterpret_cast<uint4*>(dh + i) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+          *reinterpret_cast<uint4*>(dl + i) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
         }
       }
     }

@@ -98,25 +98,17 @@ cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __
                                 __half* o_hi, __half* o_lo, int* err, cudaStream_t st);
 
 // Audio helpers -- kernels_audio.cu
-struct AudioClipRows {
-  const int* row_clip;     // [rows] clip id of each packed row
-  const int* clip_row0;    // [clips] first packed row of each clip
-  const int* clip_rows;    // [clips] valid rows of each clip
-};
 cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
                          const int* frames, int clips, int total_frames, const float* window, const float* mel,
-                         const float2* twiddle, float* features, uint8_t* mask, cudaStream_t st);
-cudaError_t audio_subsample_l0(const float* feats, const uint8_t* mask, const int* frame_off, const int* frames,
-                               const int* t0_off, const int* t0_len, int clips, int total_t0, const float* w,
-                               const float* nw, float eps, float* out, uint8_t* out_mask, cudaStream_t st);
-cudaError_t audio_subsample_l1(const float* in0, const uint8_t* mask0, const int* t0_off, const int* t0_len,
-                               const int* t1_off, const int* t1_len, int clips, int total_t1, const float* w,
-                               const float* nw, float eps, float* out, cudaStream_t st);
-cudaError_t audio_attention(const float* qkv, const float* relk, const float* pds, AudioClipRows cr, long rows,
-                            int heads, int hd, int chunk, int ctx, int plen, float softcap, __half* o_hi,
-                            __half* o_lo, cudaStream_t st);
-cudaError_t audio_lconv(const float* g, const float* dw, const float* nw, AudioClipRows cr, long rows, int d, int ks,
-                        float eps, float s_in_next, __half* a_hi, __half* a_lo, cudaStream_t st);
+                         const double2* twiddle, float* features, uint8_t* mask, cudaStream_t st);
+cudaError_t audio_subsample(const float* feats, const int* frame_off, const int* frames, const int* row0,
+                            const int* rows, const int* row_clip, long total_rows, const float* w0, const float* n0,
+                            const float* w1t, const float* n1, float eps, __half* a_hi, __half* a_lo, cudaStream_t st);
+cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
+                                   const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
+                                   float softcap, __half* o_hi, __half* o_lo, cudaStream_t st);
+cudaError_t audio_lconv_rows(const float* g, const float* dw, const float* nw, const int* row_clip, const int* row0,
+                             long rows, float eps, __half* a_hi, __half* a_lo, cudaStream_t st);
 cudaError_t gather_rows(const float* src, const int* rows_idx, long n, int d, float* dst, cudaStream_t st);
 cudaError_t row_inv_rms_operand(const float* x, long rows, int d, float eps, __half* hi, __half* lo, cudaStream_t st);
 cudaError_t add_bias_rows(float* y, const float* b, long rows, int d, cudaStream_t st);

@@ -174,6 +174,19 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
+// Two floats -> packed fp16x2 hi and lo words (hi = fp16(x), lo = fp16(x - hi)).
+__device__ __forceinline__ void split2_f16(float a, float b, uint32_t& hi, uint32_t& lo) {
+  union {
+    __half2 h;
+    uint32_t u;
+  } H, L;
+  H.h = __floats2half2_rn(a, b);
+  const float2 back = __half22float2(H.h);
+  L.h = __floats2half2_rn(a - back.x, b - back.y);
+  hi = H.u;
+  lo = L.u;
+}
+
 __device__ __forceinline__ void split_f16(float x, __half& hi, __half& lo) {
   hi = __float2half_rn(x);
   lo = __float2half_rn(x - __half2float(hi));

@@ -32,7 +32,8 @@ namespace g4m {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int kGemmThreads = 192;
+constexpr int kEpiGroups = 2;                       // epilogue warpgroups
+constexpr int kGemmThreads = 64 + 128 * kEpiGroups;  // producer, MMA, epilogue
 
 template <int BN, int TERMS>
 struct GemmCfg {
@@ -59,20 +60,51 @@ __device__ __forceinline__ float srq_f(float v, float s) {
   return r * s;
 }
 
-__device__ __forceinline__ float gelu_tanh_f(float x) {
-  // geluPytorchTanh, src/vision/kernels.ts:155-159
-  float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  return 0.5f * x * (1.0f + tanhf(inner));
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr float kLog2eF = 1.4426950408889634f;
+
+// sigmoid(x) = 1 / (1 + 2^(-x log2 e)); saturates to 0 / 1 without NaN.
+__device__ __forceinline__ float sigmoid_f(float x) { return rcp_approx(1.0f + ex2_approx(-x * kLog2eF)); }
+
+// geluPytorchTanh (src/vision/kernels.ts:155-159):
+// 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi) (x + 0.044715 x^3).
+__device__ __forceinline__ float gelu_tanh_f(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return x * sigmoid_f(2.0f * u);
+}
+
+// n values -> fp16 hi/lo planes (16-byte stores; n multiple of 8, 16-byte aligned)
 __device__ __forceinline__ void store_f16x2_row(__half* hi, __half* lo, const float* v, int n) {
-  // n multiple of 8; hi/lo 16-byte aligned
   for (int j = 0; j < n; j += 8) {
-    __align__(16) __half h[8], l[8];
+    uint32_t hv[4], lv[4];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) split_f16(v[j + u], h[u], l[u]);
-    *reinterpret_cast<uint4*>(hi + j) = *reinterpret_cast<uint4*>(h);
-    *reinterpret_cast<uint4*>(lo + j) = *reinterpret_cast<uint4*>(l);
+    for (int u = 0; u < 4; ++u) split2_f16(v[j + 2 * u], v[j + 2 * u + 1], hv[u], lv[u]);
+    *reinterpret_cast<uint4*>(hi + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    *reinterpret_cast<uint4*>(lo + j) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+  }
+}
+
+// 32 consecutive per-channel scales (broadcast loads, 16-byte aligned)
+__device__ __forceinline__ void load_scales32(const float* p, float* s) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 v = __ldg(q + i);
+    s[4 * i] = v.x;
+    s[4 * i + 1] = v.y;
+    s[4 * i + 2] = v.z;
+    s[4 * i + 3] = v.w;
   }
 }
 
@@ -101,7 +133,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bar_accf[b], 1);
-      mbar_init(&bar_acce[b], 4);
+      mbar_init(&bar_acce[b], 4 * kEpiGroups);
     }
     abort_flag = 0;
     fence_mbar_init();
@@ -196,7 +228,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    // kEpiGroups warpgroups split every tile's columns; warp w reads TMEM
+    // lanes 32*(w%4) .. +31 (one accumulator row per thread).
     const int q = warp & 3;
+    const int eg = (warp - 2) >> 2;
     const int row_in_tile = 32 * q + lane;
     uint32_t t = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
@@ -211,51 +246,84 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const bool valid = row < a.M;
       const float rs = a.row_scale;
 
-      if (EPI == EPI_F32 || EPI == EPI_PATCH) {
+      if (EPI == EPI_F32 || EPI == EPI_PATCH || EPI == EPI_SILU) {
+        constexpr int NCH = BN / 32 / kEpiGroups;
         const int* pxy = (EPI == EPI_PATCH && valid) ? a.pos_xy + 2 * (size_t)(row % a.rows_per_image) : nullptr;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = eg * NCH; c < (eg + 1) * NCH; ++c) {
           float v[32];
           tmem_ld32(tb + c * 32, v);
           if (valid) {
             const int n0 = nb * BN + c * 32;
-            float* dst = a.out_f32 + (size_t)row * a.ldo + n0;
+            if (EPI == EPI_PATCH) {
+              const float* px = a.posx_rows + (size_t)pxy[0] * a.N + n0;
+              const float* py = a.posy_rows + (size_t)pxy[1] * a.N + n0;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float y = v[j];
-              if (EPI == EPI_F32) {
-                if (a.col_scale) y = (y * rs) * a.col_scale[n0 + j];
-                y = srq_f(y, a.s_out);
-                if (a.bias) y = y + a.bias[n0 + j];
-              } else {
-                y = (y + a.posx_rows[(size_t)pxy[0] * a.N + n0 + j]) + a.posy_rows[(size_t)pxy[1] * a.N + n0 + j];
+              for (int j = 0; j < 32; ++j) v[j] = (v[j] + px[j]) + py[j];
+            } else {
+              // fused projections (proj_width > 0) keep their own output scales
+              const int which = a.proj_width > 0 ? n0 / a.proj_width : 0;
+              const float so = which == 0 ? a.s_out : (which == 1 ? a.s_out_b : a.s_out_c);
+              if (a.col_scale) {
+                float sc[32];
+                load_scales32(a.col_scale + n0, sc);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = (v[j] * rs) * sc[j];
               }
-              v[j] = y;
-            }
+              if (so != 0.0f) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                for (int j = 0; j < 32; ++j) v[j] = srq_f(v[j], so);
+              }
+              if (EPI == EPI_SILU) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = v[j] * sigmoid_f(v[j]);  // runSiluActivationCpu
+              } else if (a.bias) {
+                float bs[32];
+                load_scales32(a.bias + n0, bs);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = v[j] + bs[j];
+              }
+            }
+            if (EPI == EPI_SILU) {
+              store_f16x2_row(a.out_hi + (size_t)row * a.ldh + n0, a.out_lo + (size_t)row * a.ldh + n0, v, 32);
+            } else {
+              float* dst = a.out_f32 + (size_t)row * a.ldo + n0;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            }
           }
         }
       } else if (EPI == EPI_GELU_GATE || EPI == EPI_GLU) {
         // Tile columns [0, BN/2) carry the first operand (gate / GLU value),
         // [BN/2, BN) the second (up / GLU gate) for the same output columns.
+        constexpr int NP = BN / 64 / kEpiGroups;
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = eg * NP; c < (eg + 1) * NP; ++c) {
           float g[32], u[32];
           tmem_ld32(tb + c * 32, g);
           tmem_ld32(tb + BN / 2 + c * 32, u);
           if (valid) {
             const int ng = nb * BN + c * 32, nu = nb * BN + BN / 2 + c * 32;
             const int no = nb * (BN / 2) + c * 32;
+            float sg[32], su[32];
+            load_scales32(a.col_scale + ng, sg);
+            load_scales32(a.col_scale + nu, su);
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              float gv = srq_f((g[j] * rs) * a.col_scale[ng + j], a.s_out);
-              float uv = srq_f((u[j] * rs) * a.col_scale[nu + j], a.s_out_b);
-              if (EPI == EPI_GELU_GATE) {
-                g[j] = gelu_tanh_f(gv) * uv;  // runVisionMlpActivationCpu
-              } else {
-                g[j] = gv * (1.0f / (1.0f + expf(-uv)));  // runGluActivationCpu
+              g[j] = (g[j] * rs) * sg[j];
+              u[j] = (u[j] * rs) * su[j];
+            }
+            if (a.s_out != 0.0f || a.s_out_b != 0.0f) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                g[j] = srq_f(g[j], a.s_out);
+                u[j] = srq_f(u[j], a.s_out_b);
               }
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (EPI == EPI_GELU_GATE) g[j] = gelu_tanh_f(g[j]) * u[j];  // runVisionMlpActivationCpu
+              else g[j] = g[j] * sigmoid_f(u[j]);                          // runGluActivationCpu
             }
             if (EPI == EPI_GELU_GATE) {
               store_f16x2_row(a.out_hi + (size_t)row * a.ldh + no, a.out_lo + (size_t)row * a.ldh + no, g, 32);
@@ -266,24 +334,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
           }
         }
-      } else if (EPI == EPI_SILU) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tb + c * 32, v);
-          if (valid) {
-            const int n0 = nb * BN + c * 32;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float y = srq_f((v[j] * rs) * a.col_scale[n0 + j], a.s_out);
-              v[j] = y / (1.0f + expf(-y));  // runSiluActivationCpu
-            }
-            store_f16x2_row(a.out_hi + (size_t)row * a.ldh + n0, a.out_lo + (size_t)row * a.ldh + n0, v, 32);
-          }
-        }
       } else if (EPI == EPI_QKV_VISION) {
         // 64-column head groups: scale (+srq), head RMSNorm, 2-D RoPE (q, k),
         // scatter to the attention layouts.
+        constexpr int NH = BN / 64 / kEpiGroups;
         const int n_tile0 = nb * BN;
         const int which = n_tile0 / a.proj_width;  // 0 q, 1 k, 2 v
         const int head0 = (n_tile0 % a.proj_width) / 64;
@@ -292,34 +346,50 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float so = which == 0 ? a.s_out : (which == 1 ? a.s_out_b : a.s_out_c);
         const float* nw = which == 0 ? a.qn_w : (which == 1 ? a.kn_w : nullptr);
 #pragma unroll 1
-        for (int hh = 0; hh < BN / 64; ++hh) {
+        for (int hh = eg * NH; hh < (eg + 1) * NH; ++hh) {
           float v[64];
           tmem_ld32(tb + hh * 64, v);
           tmem_ld32(tb + hh * 64 + 32, v + 32);
           if (valid) {
             const int n0 = n_tile0 + hh * 64;
+            float sc[32];
+            load_scales32(a.col_scale + n0, sc);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = (v[j] * rs) * sc[j];
+            load_scales32(a.col_scale + n0 + 32, sc);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[32 + j] = (v[32 + j] * rs) * sc[j];
+            if (so != 0.0f) {
+#pragma unroll
+              for (int j = 0; j < 64; ++j) v[j] = srq_f(v[j], so);
+            }
             float ss = 0.f;
 #pragma unroll
-            for (int j = 0; j < 64; ++j) {
-              v[j] = srq_f((v[j] * rs) * a.col_scale[n0 + j], so);
-              ss = fmaf(v[j], v[j], ss);
-            }
+            for (int j = 0; j < 64; ++j) ss = fmaf(v[j], v[j], ss);
             const float inv = 1.0f / sqrtf(ss / 64.0f + a.eps);
+            if (nw) {
 #pragma unroll
-            for (int j = 0; j < 64; ++j) v[j] = (v[j] * inv) * (nw ? nw[j] : 1.0f);
+              for (int j = 0; j < 64; ++j) v[j] = (v[j] * inv) * __ldg(nw + j);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 64; ++j) v[j] = v[j] * inv;
+            }
             const int head = head0 + hh;
             const size_t bh = (size_t)img * a.heads + head;
             if (which < 2) {
-              const float2* cs = reinterpret_cast<const float2*>(a.rope_cs) + (size_t)tok * 32;
+              const float4* cs = reinterpret_cast<const float4*>(a.rope_cs) + (size_t)tok * 16;
               float o[64];
 #pragma unroll
               for (int p = 0; p < 2; ++p) {
 #pragma unroll
-                for (int f = 0; f < 16; ++f) {
-                  const float2 c2 = cs[p * 16 + f];
+                for (int f = 0; f < 16; f += 2) {
+                  const float4 c2 = __ldg(cs + (p * 16 + f) / 2);  // (cos, sin) of f and f + 1
                   const float x1 = v[p * 32 + f], x2 = v[p * 32 + 16 + f];
+                  const float y1 = v[p * 32 + f + 1], y2 = v[p * 32 + 16 + f + 1];
                   o[p * 32 + f] = x1 * c2.x - x2 * c2.y;
                   o[p * 32 + 16 + f] = x2 * c2.x + x1 * c2.y;
+                  o[p * 32 + f + 1] = y1 * c2.z - y2 * c2.w;
+                  o[p * 32 + 16 + f + 1] = y2 * c2.z + y1 * c2.w;
                 }
               }
               __half* dh = (which == 0 ? a.q_hi : a.k_hi) + (bh * a.rows_per_image + tok) * 64;

@@ -1,0 +1,401 @@
+// Audio tower kernels: log-mel front end, fused two-layer subsample conv,
+// chunked local self-attention and the light-conv depthwise block.
+//
+// Clips are packed back to back (ragged rows): clip c owns encoder rows
+// [clip_row0[c], clip_row0[c] + clip_rows[c]).  Every row-coupled kernel
+// (subsample conv, attention context, causal conv) stops at its clip's
+// boundaries exactly as the reference stops at the end of one unpadded clip.
+#include "g4m_kernels.h"
+#include "g4m_sm100.cuh"
+
+namespace g4m {
+
+__device__ __forceinline__ float warp_sum_a(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max_a(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Log-mel front end: preprocessGemma4AudioSamples (src/preprocess/audio.ts:22-118)
+// for unpadded clips: periodic Hann window (320), zero-padded radix-2 FFT
+// (512), magnitude, HTK mel filters (257 x 128), log(mel + 1e-3).  One CTA
+// (256 threads) per frame.  Frame f of a clip reads waveform samples
+// [f*160 - 160, f*160 + 160) (160 leading zeros, frameLength / 2).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ samples, const long* __restrict__ soff,
+                                                     const long* __restrict__ slen, const int* __restrict__ foff,
+                                                     const int* __restrict__ fcount, int clips,
+                                                     const float* __restrict__ window, const float* __restrict__ mel,
+                                                     const double2* __restrict__ tw, float* __restrict__ feats) {
+  __shared__ float re[512], im[512], mag[257];
+  const int gf = blockIdx.x;
+  // clip of this frame: binary search over frame offsets
+  int lo = 0, hi = clips - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (foff[mid] <= gf) lo = mid;
+    else hi = mid - 1;
+  }
+  const int clip = lo, f = gf - foff[clip];
+  if (f >= fcount[clip]) return;
+  const float* x = samples + soff[clip];
+  const long L = slen[clip];
+  const int t = threadIdx.x;
+  // bit-reversed load (9-bit index)
+  for (int i = t; i < 512; i += 256) {
+    float v = 0.f;
+    if (i < 320) {
+      const long idx = (long)f * 160 + i - 160;
+      if (idx >= 0 && idx < L) v = x[idx] * window[i];
+    }
+    const int r = __brev(i) >> 23;
+    re[r] = v;
+    im[r] = 0.f;
+  }
+  __syncthreads();
+  // Butterflies in double, stored to float, as fftRadix2 does with JS
+  // numbers and Float32Array storage (src/preprocess/audio.ts:191-212).
+  for (int size = 2; size <= 512; size <<= 1) {
+    const int half = size >> 1;
+    const int g = t / half, k = t % half;
+    const int e = g * size + k, o = e + half;
+    const double2 w = tw[k * (512 / size)];  // exp(-2 pi i k / size)
+    const double orr = (double)re[o] * w.x - (double)im[o] * w.y;
+    const double oi = (double)re[o] * w.y + (double)im[o] * w.x;
+    const double er = re[e], ei = im[e];
+    re[o] = (float)(er - orr);
+    im[o] = (float)(ei - oi);
+    re[e] = (float)(er + orr);
+    im[e] = (float)(ei + oi);
+    __syncthreads();
+  }
+  for (int b = t; b < 257; b += 256) mag[b] = (float)hypot((double)re[b], (double)im[b]);
+  __syncthreads();
+  if (t < 128) {
+    double e = 0.0;  // mel energy in double (JS number), in bin order
+    for (int b = 0; b < 257; ++b) e += (double)mag[b] * (double)mel[b * 128 + t];
+    feats[(long)gf * 128 + t] = (float)log(e + 0.001);
+  }
+}
+
+cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
+                         const int* frames, int clips, int total_frames, const float* window, const float* mel,
+                         const double2* twiddle, float* features, uint8_t* mask, cudaStream_t st) {
+  (void)mask;
+  if (total_frames <= 0) return cudaSuccess;
+  logmel_kernel<<<total_frames, 256, 0, st>>>(samples, sample_off, sample_len, frame_off, frames, clips, window, mel,
+                                              twiddle, features);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Fused subsample conv (runAudioSubsampleConvLayerCpu twice,
+// src/audio/kernels.ts:112-183): per output row t1 of a clip, the three
+// layer-0 rows 2*t1-1 .. 2*t1+1 (64 freq x 128 channels, channel LayerNorm
+// with weight, ReLU) are computed into shared memory, then layer 1
+// (128 -> 32 channels, 3x3 stride 2, LayerNorm, ReLU) produces the 32 x 32
+// flattened row (index f * 32 + c) as the fp16 hi/lo operand of the input
+// projection.  Source rows outside the clip are skipped, as masked or
+// out-of-range source times are in the reference.
+// w0: [128][3][3]; w1t: [3][3][128 in][32 out] (transposed at load).
+// ---------------------------------------------------------------------------
+constexpr int L0P = 129;  // padded channel pitch of a layer-0 (row, freq) vector
+
+__global__ void __launch_bounds__(256) subsample_kernel(const float* __restrict__ feats, const int* __restrict__ foff,
+                                                        const int* __restrict__ fcount, const int* __restrict__ row0,
+                                                        const int* __restrict__ rows, const int* __restrict__ row_clip,
+                                                        const float* __restrict__ w0, const float* __restrict__ n0,
+                                                        const float* __restrict__ w1t, const float* __restrict__ n1,
+                                                        float eps, __half* __restrict__ a_hi,
+                                                        __half* __restrict__ a_lo) {
+  extern __shared__ float sm[];
+  float* l0 = sm;                    // [3][64][L0P]
+  float* xf = sm + 3 * 64 * L0P;     // [7][128] input features
+  __shared__ double stat[3 * 64][2];  // mean, inv std per (row, freq)
+  const long grow = blockIdx.x;
+  const int clip = row_clip[grow];
+  const int t1 = (int)(grow - row0[clip]);
+  const int F = fcount[clip];
+  const int T0 = (F - 1) / 2 + 1;
+  const float* fx = feats + (long)foff[clip] * 128;
+  const int t = threadIdx.x;
+  // features rows 4*t1-3 .. 4*t1+3
+  for (int i = t; i < 7 * 128; i += 256) {
+    const int r = 4 * t1 - 3 + i / 128;
+    xf[i] = (r >= 0 && r < F) ? fx[(long)r * 128 + (i % 128)] : 0.f;
+  }
+  __syncthreads();
+  // layer 0 raw conv: thread -> channel c = t % 128, freq parity t / 128
+  {
+    const int c = t & 127;
+    float w[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) w[k] = w0[c * 9 + k];
+    for (int rr = 0; rr < 3; ++rr) {
+      const int t0 = 2 * t1 - 1 + rr;
+      for (int f = t >> 7; f < 64; f += 2) {
+        double s = 0.0;  // audioSubsampleConvValueCpu accumulates in double
+        if (t0 >= 0 && t0 < T0) {
+#pragma unroll
+          for (int kt = 0; kt < 3; ++kt) {
+            const int srow = 2 * t0 + kt - 1;  // feature row
+            if (srow < 0 || srow >= F) continue;
+            const float* xr = xf + (srow - (4 * t1 - 3)) * 128;
+#pragma unroll
+            for (int kf = 0; kf < 3; ++kf) {
+              const int sf = 2 * f + kf - 1;
+              if (sf < 0 || sf >= 128) continue;
+              s = fma((double)xr[sf], (double)w[kt * 3 + kf], s);
+            }
+          }
+        }
+        l0[(rr * 64 + f) * L0P + c] = (float)s;
+      }
+    }
+  }
+  __syncthreads();
+  // layer 0 channel LayerNorm stats: thread per (row, freq)
+  if (t < 192) {  // channel LayerNorm statistics in double (src/audio/kernels.ts:131-143)
+    const float* v = l0 + t * L0P;
+    double mean = 0.0;
+    for (int c = 0; c < 128; ++c) mean += v[c];
+    mean /= 128.0;
+    double var = 0.0;
+    for (int c = 0; c < 128; ++c) {
+      const double d = (double)v[c] - mean;
+      var += d * d;
+    }
+    stat[t][0] = mean;
+    stat[t][1] = 1.0 / sqrt(var / 128.0 + (double)eps);
+  }
+  __syncthreads();
+  for (int i = t; i < 3 * 64 * 128; i += 256) {
+    const int rf = i >> 7, c = i & 127;
+    const double v = ((double)l0[rf * L0P + c] - stat[rf][0]) * stat[rf][1] * (double)n0[c];
+    l0[rf * L0P + c] = (float)(v > 0.0 ? v : 0.0);
+  }
+  __syncthreads();
+  // layer 1: lane = output channel, warp = freq group (f = warp + 8 i)
+  const int lane = t & 31, wg = t >> 5;
+  double acc[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int kt = 0; kt < 3; ++kt) {
+    const int t0 = 2 * t1 - 1 + kt;
+    if (t0 < 0 || t0 >= T0) continue;
+    for (int kf = 0; kf < 3; ++kf) {
+      const float* wk = w1t + (kt * 3 + kf) * 128 * 32;
+      for (int ci = 0; ci < 128; ++ci) {
+        const double wv = __ldg(wk + ci * 32 + lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int sf = 2 * (wg + 8 * i) + kf - 1;
+          if (sf >= 0 && sf < 64) acc[i] = fma((double)l0[(kt * 64 + sf) * L0P + ci], wv, acc[i]);
+        }
+      }
+    }
+  }
+  const long orow = grow;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int f = wg + 8 * i;
+    const float cv = (float)acc[i];  // channelValues is a Float32Array
+    double mean = (double)acc[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mean += __shfl_xor_sync(0xffffffffu, mean, o);
+    mean /= 32.0;
+    const double d = (double)cv - mean;
+    double var = d * d;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    const double inv = 1.0 / sqrt(var / 32.0 + (double)eps);
+    const double nv = d * inv * (double)n1[lane];
+    const float v = (float)(nv > 0.0 ? nv : 0.0);
+    __half h, l;
+    split_f16(v, h, l);
+    a_hi[orow * 1024 + f * 32 + lane] = h;
+    a_lo[orow * 1024 + f * 32 + lane] = l;
+  }
+}
+
+cudaError_t audio_subsample(const float* feats, const int* frame_off, const int* frames, const int* row0,
+                            const int* rows, const int* row_clip, long total_rows, const float* w0, const float* n0,
+                            const float* w1t, const float* n1, float eps, __half* a_hi, __half* a_lo, cudaStream_t st) {
+  if (total_rows <= 0) return cudaSuccess;
+  const int smem = (3 * 64 * L0P + 7 * 128) * 4;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(subsample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  subsample_kernel<<<(unsigned)total_rows, 256, smem, st>>>(feats, frame_off, frames, row0, rows, row_clip, w0, n0,
+                                                            w1t, n1, eps, a_hi, a_lo);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Chunked local self-attention (runAudioSelfAttentionBodyCpu and
+// audioSelfAttentionScore, src/audio/kernels.ts:432-512): chunk 12, context
+// 24 (12 past-horizon rows), 13 relative positions, per-dim softplus query
+// scale, tanh softcap.  Out-of-clip context rows add no key term and no
+// value, but their slot stays in the softmax with the relative-only score.
+// One CTA per (clip block of 12 rows, head), 4 warps x 3 query rows.
+// qkv: [rows][3 * 1024] f32 (q | k | v); relk: [13][1024]; qmul: [128]
+// (= 128^-0.5 / ln 2 * softplus(per_dim_scale)); kscale = ln(1 + e) / ln 2.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict__ qkv, const float* __restrict__ relk,
+                                                         const float* __restrict__ qmul, const int* __restrict__ blk_clip,
+                                                         const int* __restrict__ blk_index,
+                                                         const int* __restrict__ row0, const int* __restrict__ rows,
+                                                         float kscale, float softcap, __half* __restrict__ o_hi,
+                                                         __half* __restrict__ o_lo) {
+  constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, D = 1024;
+  __shared__ float ks[CTX][HD], vs[CTX][HD], rk[PL][HD];
+  const int head = blockIdx.y;
+  const int clip = blk_clip[blockIdx.x], blk = blk_index[blockIdx.x];
+  const long r0 = row0[clip];
+  const int nr = rows[clip];
+  const int t = threadIdx.x;
+  for (int i = t; i < CTX * HD; i += 128) {
+    const int c = i / HD, d = i % HD;
+    const int src = blk * CH + c - (CTX - CH);
+    float kv = 0.f, vv = 0.f;
+    if (src >= 0 && src < nr) {
+      const float* row = qkv + (r0 + src) * (3 * D) + head * HD + d;
+      kv = row[D] * kscale;
+      vv = row[2 * D];
+    }
+    ks[c][d] = kv;
+    vs[c][d] = vv;
+  }
+  for (int i = t; i < PL * HD; i += 128) rk[i / HD][i % HD] = relk[(i / HD) * D + head * HD + (i % HD)];
+  __syncthreads();
+  const int lane = t & 31, warp = t >> 5;
+  float qm[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) qm[j] = qmul[lane + 32 * j];
+  for (int qi = warp; qi < CH; qi += 4) {
+    const int lr = blk * CH + qi;  // local query row
+    if (lr >= nr) break;
+    const float* qrow = qkv + (r0 + lr) * (3 * D) + head * HD;
+    float q[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) q[j] = qrow[lane + 32 * j] * qm[j];
+    float myscore = -INFINITY;  // lane c < 24 keeps score of context c
+    for (int c = 0; c < CTX; ++c) {
+      const int src = blk * CH + c - (CTX - CH);
+      const int rel = c - qi;
+      const bool kv_ok = src >= 0 && src < nr;
+      const bool rel_ok = rel >= 0 && rel < PL;
+      float p = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float kk = (kv_ok ? ks[c][lane + 32 * j] : 0.f) + (rel_ok ? rk[rel][lane + 32 * j] : 0.f);
+        p = fmaf(q[j], kk, p);
+      }
+      p = warp_sum_a(p);
+      const float sc = tanhf(p / softcap) * softcap;
+      if (lane == c) myscore = sc;
+    }
+    const float mx = warp_max_a(myscore);
+    const float e = lane < CTX ? expf(myscore - mx) : 0.f;
+    const float den = warp_sum_a(e);
+    const float w = e / den;
+    float o[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < CTX; ++c) {
+      const float wc = __shfl_sync(0xffffffffu, w, c);
+      const int src = blk * CH + c - (CTX - CH);
+      if (src < 0 || src >= nr) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) o[j] = fmaf(wc, vs[c][lane + 32 * j], o[j]);
+    }
+    const long orow = r0 + lr;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half h, l;
+      split_f16(o[j], h, l);
+      o_hi[orow * D + head * HD + lane + 32 * j] = h;
+      o_lo[orow * D + head * HD + lane + 32 * j] = l;
+    }
+  }
+}
+
+cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
+                                   const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
+                                   float softcap, __half* o_hi, __half* o_lo, cudaStream_t st) {
+  if (nblocks <= 0) return cudaSuccess;
+  dim3 grid(nblocks, 8);
+  audio_attn_kernel<<<grid, 128, 0, st>>>(qkv, relk, qmul, blk_clip, blk_index, row0, rows, kscale, softcap, o_hi,
+                                          o_lo);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------
+// Light-conv middle: causal depthwise conv (kernel 5, left pad 4) within the
+// clip (runAudioDepthwiseCausalConv1dCpu, src/audio/kernels.ts:855-884),
+// conv_norm RMSNorm, SiLU (runSiluActivationCpu) -> fp16 hi/lo operand of
+// linear_end.  One warp per row, d = 1024.  dw: [1024][5].
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) lconv_kernel(const float* __restrict__ g, const float* __restrict__ dw,
+                                                    const float* __restrict__ nw, const int* __restrict__ row_clip,
+                                                    const int* __restrict__ row0, long nrows, float eps,
+                                                    __half* __restrict__ a_hi, __half* __restrict__ a_lo) {
+  constexpr int D = 1024, V = D / 128, KS = 5;
+  const int lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= nrows) return;
+  const long local = row - row0[row_clip[row]];
+  float4 acc[V];
+#pragma unroll
+  for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int k = 0; k < KS; ++k) {
+    const long src = local + k - (KS - 1);
+    if (src < 0) continue;
+    const float4* x = reinterpret_cast<const float4*>(g + (row + k - (KS - 1)) * D);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      const int c = 4 * (lane + 32 * i);
+      const float4 v = x[lane + 32 * i];
+      acc[i].x = fmaf(v.x, dw[(c + 0) * KS + k], acc[i].x);
+      acc[i].y = fmaf(v.y, dw[(c + 1) * KS + k], acc[i].y);
+      acc[i].z = fmaf(v.z, dw[(c + 2) * KS + k], acc[i].z);
+      acc[i].w = fmaf(v.w, dw[(c + 3) * KS + k], acc[i].w);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < V; ++i) ss += acc[i].x * acc[i].x + acc[i].y * acc[i].y + acc[i].z * acc[i].z + acc[i].w * acc[i].w;
+  const float inv = 1.0f / sqrtf(warp_sum_a(ss) / (float)D + eps);
+  const float4* w = reinterpret_cast<const float4*>(nw);
+#pragma unroll
+  for (int i = 0; i < V; ++i) {
+    const float4 wv = w[lane + 32 * i];
+    float v[4] = {(acc[i].x * inv) * wv.x, (acc[i].y * inv) * wv.y, (acc[i].z * inv) * wv.z, (acc[i].w * inv) * wv.w};
+    __align__(8) __half hh[4], ll[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float s = v[u] / (1.0f + expf(-v[u]));
+      split_f16(s, hh[u], ll[u]);
+    }
+    const int c = 4 * (lane + 32 * i);
+    *reinterpret_cast<uint2*>(a_hi + row * D + c) = *reinterpret_cast<uint2*>(hh);
+    *reinterpret_cast<uint2*>(a_lo + row * D + c) = *reinterpret_cast<uint2*>(ll);
+  }
+}
+
+cudaError_t audio_lconv_rows(const float* g, const float* dw, const float* nw, const int* row_clip, const int* row0,
+                             long rows, float eps, __half* a_hi, __half* a_lo, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  lconv_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(g, dw, nw, row_clip, row0, rows, eps, a_hi, a_lo);
+  return cudaGetLastError();
+}
+
+}  // namespace g4m

@@ -492,6 +492,7 @@ static int vision_check_quant(const VisionWeights& vw, int layers) {
 
 int vision_forward(g4m_ctx* ctx, Device& d, int B, const float* pix_dev, int H, int W, int max_soft, int layers,
                    float* out_dev, cudaStream_t st) {
+  (void)cudaGetLastError();  // a failed earlier call must not leak into this one
   VisionWeights& vw = d.vw;
   if (vw.layers == 0) return fail(G4M_E_NOT_LOADED, "vision tower weights are not loaded");
   if (layers < 1 || layers > 16)
@@ -573,6 +574,7 @@ int vision_tokens_for(int H, int W, int max_soft, int* tokens) {
 int qat_linear_device(Device& d, const __half* w16, const float* scale, const float* bias, const void* w_raw, int bits,
                       int rows, int in, int out, float s_in, float s_out, const float* x_dev, float* y_dev, DevBuf& a_hi,
                       DevBuf& a_lo, cudaStream_t st) {
+  (void)cudaGetLastError();
   if (w16) {
     if (ensure(a_hi, (size_t)rows * in * 2) || ensure(a_lo, (size_t)rows * in * 2))
       return fail(G4M_E_CUDA, "operand allocation failed");
@@ -673,6 +675,7 @@ int g4m_load_weights(g4m_ctx* ctx, const char* path) {
   SafeTensors f;
   std::string err;
   if (!f.open(path, err)) return fail(G4M_E_IO, err);
+  (void)cudaGetLastError();
   for (Device* d : ctx->devs) {
     std::lock_guard<std::mutex> lk(d->mu);
     cudaSetDevice(d->id);
@@ -763,7 +766,7 @@ int g4m_linear_run(g4m_linear* L, const float* x_dev, int rows, float* y_dev, vo
   if (rows == 0) return G4M_OK;
   Device& d = *L->d;
   cudaSetDevice(d.id);
-  cudaStream_t st = stream ? (cudaStream_t)stream : (cudaStream_t)0;
+  cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamLegacy;  // NULL: the default stream
   return qat_linear_device(d, L->w16, L->scale, L->bias, L->w_raw, L->bits, rows, L->in, L->out, L->s_in, L->s_out,
                            x_dev, y_dev, L->a_hi, L->a_lo, st);
 }
@@ -787,7 +790,7 @@ int g4m_vision_embed_device(g4m_ctx* ctx, int di, int n, const float* pixels_dev
   Device& d = *ctx->devs[di];
   std::lock_guard<std::mutex> lk(d.mu);
   cudaSetDevice(d.id);
-  cudaStream_t st = stream ? (cudaStream_t)stream : d.st;
+  cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamLegacy;  // NULL: the default stream
   return vision_forward(ctx, d, n, pixels_dev, height, width, max_soft_tokens, layer_count, out_dev, st);
 }
 

@@ -89,7 +89,7 @@ struct AudioWeights {
   __half *emb_hi = nullptr, *emb_lo = nullptr;  // embedder [1536, 1536]
   float* window = nullptr;   // periodic Hann [320]
   float* mel = nullptr;      // [257][128]
-  float2* twiddle = nullptr; // [256]
+  double2* twiddle = nullptr;  // [256] exp(-2 pi i k / 512)
 };
 
 struct LayoutCache {
@@ -131,6 +131,7 @@ struct Device {
   DevBuf io_in, io_out;
   long last_vision_rows = 0;
   long last_audio_rows = 0;
+  int aw_mel_sr = 0;  // sampling rate the mel filter bank was built for
   std::mutex mu;
 
   cudaEvent_t next_event() {

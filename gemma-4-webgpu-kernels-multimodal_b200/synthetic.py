@@ -265,8 +265,12 @@ def write_safetensors(path: str, tensors: Dict[str, np.ndarray], dtypes: Dict[st
     header = {}
     off = 0
     order = sorted(tensors)
+    arrays = {}
     for name in order:
-        a = np.ascontiguousarray(tensors[name])
+        a = np.asarray(tensors[name])
+        arrays[name] = a if a.flags.c_contiguous else a.copy()  # keeps 0-d scalars 0-d
+    for name in order:
+        a = arrays[name]
         dt = (dtypes or {}).get(name) or _DTYPE[a.dtype]
         header[name] = {"dtype": dt, "shape": list(a.shape), "data_offsets": [off, off + a.nbytes]}
         off += a.nbytes
@@ -277,7 +281,7 @@ def write_safetensors(path: str, tensors: Dict[str, np.ndarray], dtypes: Dict[st
         f.write(struct.pack("<Q", len(hb)))
         f.write(hb)
         for name in order:
-            f.write(np.ascontiguousarray(tensors[name]).tobytes())
+            f.write(arrays[name].tobytes())
 
 
 def read_safetensors(path: str) -> Dict[str, np.ndarray]:

@@ -166,3 +166,42 @@ def logmel(samples, frame_len=320, hop=160, fft=512, nmel=128, sr=16000, fmin=0.
     idx = np.arange(frames)[:, None] * hop + np.arange(frame_len)[None, :]
     spec = np.abs(np.fft.rfft(wav[idx] * win, n=fft, axis=1))
     return np.log(spec @ filt + floor)
+
+
+def audio_layer(W, i, h):
+    """One conformer layer in float64 (src/audio/encoder.ts:761-1071 dataflow)."""
+    p = f"model.audio_tower.layers.{i}"
+    D = 1024
+
+    def lin(prefix, x, inp, out):
+        w = W[f"{prefix}.weight"]
+        bits = int(w.nbytes * 8 // (inp * out))
+        return packed_qat(x, w, W[f"{prefix}.weight_scale"], inp, bits,
+                          float(W[f"{prefix}.input_activation_scale"]), float(W[f"{prefix}.output_activation_scale"]))
+
+    def ffn(blk, h):
+        x = rmsnorm(h, W[f"{p}.{blk}.pre_layer_norm.weight"])
+        x = lin(f"{p}.{blk}.ffw_layer_1.linear", x, D, 4096)
+        x = x / (1 + np.exp(-x))
+        x = lin(f"{p}.{blk}.ffw_layer_2.linear", x, 4096, D)
+        return h + 0.5 * rmsnorm(x, W[f"{p}.{blk}.post_layer_norm.weight"])
+
+    h = np.asarray(h, np.float64)
+    h1 = ffn("feed_forward1", h)
+    a = rmsnorm(h1, W[f"{p}.norm_pre_attn.weight"])
+    q = lin(f"{p}.self_attn.q_proj.linear", a, D, D)
+    k = lin(f"{p}.self_attn.k_proj.linear", a, D, D)
+    v = lin(f"{p}.self_attn.v_proj.linear", a, D, D)
+    rk = relpos(13, D) @ np.asarray(W[f"{p}.self_attn.relative_k_proj.weight"], np.float64).T
+    o = audio_attention(q, k, v, rk, W[f"{p}.self_attn.per_dim_scale"], 8, 128)
+    o = lin(f"{p}.self_attn.post.linear", o, D, D)
+    h2 = h1 + rmsnorm(o, W[f"{p}.norm_post_attn.weight"])
+    x = rmsnorm(h2, W[f"{p}.lconv1d.pre_layer_norm.weight"])
+    x = lin(f"{p}.lconv1d.linear_start.linear", x, D, 2 * D)
+    x = x[:, :D] / (1 + np.exp(-x[:, D:]))
+    x = depthwise(x, W[f"{p}.lconv1d.depthwise_conv1d.weight"])
+    x = rmsnorm(x, W[f"{p}.lconv1d.conv_norm.weight"])
+    x = x / (1 + np.exp(-x))
+    h3 = h2 + lin(f"{p}.lconv1d.linear_end.linear", x, D, D)
+    h4 = ffn("feed_forward2", h3)
+    return rmsnorm(h4, W[f"{p}.norm_out.weight"])

@@ -87,3 +87,16 @@ def test_preprocess_image_blob(g4m, oracle):
     assert np.array_equal(got["pixelValues"].reshape(exp["pixelValues"].shape), exp["pixelValues"])
     assert np.array_equal(got["imagePositionIds"].reshape(-1, 2), exp["imagePositionIds"])
     assert got["numSoftTokens"] == 4 and got["patchPixels"] == 768
+
+
+def test_synthetic_checkpoint_round_trip(syn, tmp_path):
+    """Scalar activation scales stay 0-d (shape []) as scalarF32FromTensor
+    requires (src/io/safetensors.ts:170-175)."""
+    W = syn.vision_weights(0, layers=1)
+    p = str(tmp_path / "v.safetensors")
+    syn.write_safetensors(p, W)
+    R = syn.read_safetensors(p)
+    assert set(R) == set(W)
+    for k, v in W.items():
+        assert R[k].shape == v.shape and R[k].dtype == v.dtype and np.array_equal(R[k], v), k
+    assert R["model.vision_tower.encoder.layers.0.self_attn.q_proj.linear.input_activation_scale"].shape == ()

@@ -1,0 +1,193 @@
+"""GPU parity of the audio tower (log-mel -> subsample convs -> conformer
+layers -> output projection -> embedder) against the oracle's restatement of
+the reference CPU twins (computeGemma4AudioEmbeddings dataflow).
+
+The random-init audio tower is chaotic: its attention scores reach ~1e3
+before the tanh softcap, so relative noise of ~1e-6 in q and k (the level of
+the reference's own f32 sequential sums) changes scores by ~1e-3 and the
+softmax amplifies it.  Perturbing the oracle's own encoder input by 1e-7
+drives the oracle to a row cosine of ~0.35 against itself after 12 layers.
+The north-star tolerance is therefore asserted per layer (layer-anchored, as
+the reference's paired probes do) and on one- and two-layer stacks; the
+12-layer propagated run is compared with the oracle's own divergence under a
+rounding-level input perturbation."""
+import numpy as np
+import pytest
+
+from conftest import assert_parity, row_metrics
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def aud(native, syn, tmp_path_factory):
+    W = syn.audio_weights(0, layers=2)
+    path = str(tmp_path_factory.mktemp("audio") / "audio2.safetensors")
+    syn.write_safetensors(path, W)
+    c = native.Context()
+    c.load_weights(path)
+    yield c, W, path
+    c.close()
+
+
+def sine(seconds, f1=440.0, f2=660.0, a1=0.16, a2=0.05, rate=16000):
+    """Probe-style test tone (src/audio/probes.ts:20-27)."""
+    t = np.arange(int(rate * seconds)) / rate
+    return (a1 * np.sin(2 * np.pi * f1 * t) + a2 * np.sin(2 * np.pi * f2 * t)).astype(np.float32)
+
+
+def test_audio_front_end(aud, oracle, syn):
+    """Log-mel + subsample convs + input projection (the encoder input)
+    against the oracle, tightly: the front end is computed in double where
+    the reference uses JS numbers."""
+    c, W, _ = aud
+    c.set_debug(True)
+    try:
+        for n in (16000, 37000, 1280):
+            x = syn.audio_samples(7, n)
+            pre = oracle.preprocess_audio(x, pad_to_multiple_of=None)
+            ref, _ = oracle.audio_subsample(W, pre["inputFeatures"], pre["inputFeaturesMask"])
+            c.audio_embed([x], 16000, 1)
+            got = c.audio_debug_hidden(ref.shape[0], which=0)
+            assert_parity(ref, got, cos_min=0.999999, maxabs=1e-4, what=f"front end n={n}")
+    finally:
+        c.set_debug(False)
+
+
+@pytest.mark.parametrize("n,layers", [(16000, 1), (16000, 2), (37000, 1)])
+def test_audio_small_stack(aud, oracle, syn, n, layers):
+    """Whole pipeline vs the oracle.  The north-star bound (row cosine >=
+    0.999, max-abs <= 1e-2 * RMS) is required unless the oracle itself -- the
+    reference's f32 arithmetic -- is farther than that from a float64
+    evaluation of the same layers; then the GPU must be within twice the
+    oracle's own float64 error (measured on the encoder output)."""
+    import np_ref
+    c, W, _ = aud
+    x = syn.audio_samples(1, n)
+    hid = []
+    ref = oracle.audio_embed(W, x, layer_count=layers, hidden_out=hid)
+    outs, rows = c.audio_embed([x], 16000, layers)
+    assert rows[0] == ref["validSubsampleRows"] == oracle.audio_soft_token_count(n)
+    cos, ma = row_metrics(ref["embeddings"], outs[0])
+    assert np.isfinite(outs[0]).all() and cos >= 0.999, cos
+    if ma > 1e-2:
+        h64 = np.asarray(hid[0], np.float64)
+        for i in range(layers):
+            h64 = np_ref.audio_layer(W, i, h64)
+        _, ma_ref = row_metrics(h64, hid[-1])
+        _, ma_gpu = row_metrics(h64, c.audio_debug_hidden(rows[0], which=1))
+        assert ma_gpu <= 2 * ma_ref, (ma, ma_gpu, ma_ref)
+        print(f"audio n={n} x{layers}: GPU vs oracle max-abs/RMS {ma:.3e}; vs float64: GPU {ma_gpu:.3e}, "
+              f"oracle {ma_ref:.3e}")
+
+
+def test_audio_encoder_output_anchored(aud, oracle, syn):
+    c, W, _ = aud
+    x = syn.audio_samples(2, 24000)
+    hid = []
+    oracle.audio_embed(W, x, layer_count=1, hidden_out=hid)
+    c.audio_embed([x], 16000, 1)
+    got = c.audio_debug_hidden(hid[-1].shape[0])
+    assert_parity(hid[-1], got, what="encoder output after 1 layer")
+
+
+def test_audio_probe_tones(aud, oracle):
+    """0.08 s (2 rows) and 0.02 s (1 row) tones of the reference probes."""
+    c, W, _ = aud
+    for sec, f1, f2, a1, a2 in [(0.08, 440, 660, 0.16, 0.05), (0.02, 440, 880, 0.2, 0.08)]:
+        x = sine(sec, f1, f2, a1, a2)
+        ref = oracle.audio_embed(W, x, layer_count=2)
+        outs, rows = c.audio_embed([x], 16000, 2)
+        assert rows[0] == ref["embeddings"].shape[0] == (2 if sec == 0.08 else 1)
+        assert_parity(ref["embeddings"], outs[0], what=f"tone {sec}s")
+
+
+def test_audio_ragged_batch_matches_single(aud, syn):
+    c, _, _ = aud
+    clips = [syn.audio_samples(10 + i, n) for i, n in enumerate([16000, 5000, 47000, 1280, 30000])]
+    batch, rows = c.audio_embed(clips, 16000, 2)
+    for i, x in enumerate(clips):
+        single, r = c.audio_embed([x], 16000, 2)
+        assert r[0] == rows[i]
+        assert np.array_equal(single[0], batch[i]), i
+
+
+def test_audio_errors_and_cap(aud, native, syn, oracle):
+    c, W, _ = aud
+    with pytest.raises(native.G4MError) as e:
+        c.audio_embed([np.zeros(100, np.float32)], 16000, 1)  # no frames
+    assert e.value.status == 2
+    with pytest.raises(native.G4MError) as e:
+        c.audio_embed([syn.audio_samples(0, 16000)], 16000, 3)  # checkpoint holds 2 layers
+    assert e.value.status == 8
+    x = syn.audio_samples(3, 30000)
+    capped, rows = c.audio_embed([x], 16000, 1, max_samples=16000)
+    full, _ = c.audio_embed([x[:16000]], 16000, 1)
+    assert rows[0] == 25 and np.array_equal(capped[0], full[0])
+
+
+def test_audio_public_api(aud, g4m, oracle):
+    _, W, path = aud
+    g4m.configure(path)
+    try:
+        x = sine(1.0)
+        r = g4m.computeGemma4AudioEmbeddings({"samples": x, "samplingRate": 16000, "layerCount": 2})
+        assert r["ok"] and r["rows"] == 25 and r["dim"] == 1536 and r["stages"]["frames"] == 99
+        ref = oracle.audio_embed(W, x, layer_count=2)
+        assert_parity(ref["embeddings"], r["embeddings"].reshape(25, 1536), what="public API")
+        assert r["checksum"] == oracle.checksum_floats(r["embeddings"])
+    finally:
+        g4m.close()
+
+
+@pytest.fixture(scope="module")
+def aud12(native, syn, tmp_path_factory):
+    W = syn.audio_weights(0, layers=12)
+    path = str(tmp_path_factory.mktemp("audio12") / "audio12.safetensors")
+    syn.write_safetensors(path, W)
+    c = native.Context()
+    c.load_weights(path)
+    yield c, W
+    c.close()
+
+
+def test_audio_all_layers_anchored(aud12, oracle, syn):
+    """Every conformer layer, fed the oracle's input for that layer (two clips
+    packed back to back), matches the oracle's output at the north-star
+    tolerance."""
+    c, W = aud12
+    xs = [syn.audio_samples(20, 16000), syn.audio_samples(21, 32000)]
+    hs = []
+    for x in xs:
+        pre = oracle.preprocess_audio(x, pad_to_multiple_of=None)
+        h, _ = oracle.audio_subsample(W, pre["inputFeatures"], pre["inputFeaturesMask"])
+        hs.append(h)
+    rows = [h.shape[0] for h in hs]
+    for i in range(12):
+        packed = np.concatenate(hs, 0)
+        got = c.audio_layers(packed, rows, i, 1)
+        hs = [oracle.audio_layer(W, i, h) for h in hs]
+        assert_parity(np.concatenate(hs, 0), got, what=f"audio layer {i} anchored")
+
+
+def test_audio_12_layers_propagated(aud12, oracle, syn):
+    """Full 12-layer run: finite, and no farther from the oracle than the
+    oracle is from itself when its encoder input is perturbed by 1e-6."""
+    c, W = aud12
+    x = syn.audio_samples(4, 32000)
+    ref = oracle.audio_embed(W, x, layer_count=12)
+    outs, _ = c.audio_embed([x], 16000, 12)
+    pre = oracle.preprocess_audio(x, pad_to_multiple_of=None)
+    h, _ = oracle.audio_subsample(W, pre["inputFeatures"], pre["inputFeaturesMask"])
+    h = (h * (1 + 1e-6 * np.random.default_rng(0).standard_normal(h.shape))).astype(np.float32)
+    for i in range(12):
+        h = oracle.audio_layer(W, i, h)
+    env = oracle.embedder(oracle.add_bias_rows(oracle.f32_linear_rows(h, W["model.audio_tower.output_proj.weight"]),
+                                               W["model.audio_tower.output_proj.bias"]),
+                          W["model.embed_audio.embedding_projection.weight"])
+    cos_env, ma_env = row_metrics(ref["embeddings"], env)
+    cos, ma = row_metrics(ref["embeddings"], outs[0])
+    print(f"audio 12 layers: GPU vs oracle cos {cos:.5f} max-abs/RMS {ma:.3e}; "
+          f"oracle vs 1e-6-perturbed oracle cos {cos_env:.5f} max-abs/RMS {ma_env:.3e}")
+    assert np.isfinite(outs[0]).all()
+    assert (1 - cos) <= 3 * (1 - cos_env) + 1e-3, (cos, cos_env)
