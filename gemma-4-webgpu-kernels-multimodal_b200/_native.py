@@ -36,6 +36,7 @@ _SIGS = [
     ("g4m_linear_prepare", _I, [_VP, _I, _VP, _I, _I, _I, _VP, _F, _F, _VP, ctypes.POINTER(_VP)]),
     ("g4m_linear_run", _I, [_VP, _VP, _I, _VP, _VP]),
     ("g4m_linear_free", None, [_VP]),
+    ("g4m_linear_run_noalloc", _I, [_VP, _VP, _I, _VP, _VP]),
     ("g4m_vision_embed_batch", _I, [_VP, _I, _VP, _I, _I, _I, _I, _VP, _VP, _VP]),
     ("g4m_vision_embed_device", _I, [_VP, _I, _I, _VP, _I, _I, _I, _I, _VP, _VP]),
     ("g4m_vision_debug_hidden", _I, [_VP, _I, _I, _VP, ctypes.c_size_t]),

@@ -195,6 +195,9 @@ int load_qat(Device& d, const class SafeTensors& f, const std::string& prefix, c
 std::vector<int> map_interleave(int n, int which);
 cudaError_t qat_linear_simt(const float* x, const void* w, int bits, const float* scale, const float* bias, int rows,
                             int in, int out, float s_in, float s_out, float* y, cudaStream_t st);
+int qat_linear_device(Device& d, const __half* w16, const float* scale, const float* bias, const void* w_raw, int bits,
+                      int rows, int in, int out, float s_in, float s_out, const float* x_dev, float* y_dev, DevBuf& a_hi,
+                      DevBuf& a_lo, cudaStream_t st);
 
 }  // namespace g4m
 

@@ -94,6 +94,18 @@ G4M_API int g4m_linear_prepare(g4m_ctx* ctx, int device_index, const void* w, in
 G4M_API int g4m_linear_run(g4m_linear* lin, const float* x_dev, int rows, float* y_dev, void* stream);
 G4M_API void g4m_linear_free(g4m_linear* lin);
 
+/* g4m_linear_run without any device allocation (no reference counterpart:
+ * the reference's WebGPU runner creates its buffers per call).  The fp16
+ * activation operand is staged in a static 16 MiB device array (two planes
+ * of 4,194,304 elements) instead of a per-linear buffer grown by cudaMalloc,
+ * so a call never allocates, frees or grows memory.  Limit: rows * in <=
+ * 4,194,304, else G4M_E_SHAPE and nothing is launched.  The first call on
+ * each device looks up the array's address (cudaGetSymbolAddress, which may
+ * load the module); make that first call before any stream capture.  All
+ * calls on one device share the array: calls in flight at the same time on
+ * one device race and must be serialised by the caller. */
+G4M_API int g4m_linear_run_noalloc(g4m_linear* lin, const float* x_dev, int rows, float* y_dev, void* stream);
+
 /* ------------------------------------------------------------- vision */
 
 /* Image embeddings for n images of one size (computeGemma4VisionImageEmbeddings,
