@@ -7,16 +7,32 @@
 //
 // Operands are fp16 hi/lo planes, so every product is split into three
 // tensor-core terms (hi*hi + hi*lo + lo*hi) for fp32-grade scores and
-// outputs:   S = Qh Kh^T + Qh Kl^T + Ql Kh^T,   O += Ph Vh + Ph Vl + Pl Vh.
+// outputs:   S = Qh Kh^T + Qh Kl^T + Ql Kh^T,   O += (Ph + Pl) (Vh + Vl).
+// A tcgen05.mma costs about the same for any N <= 128, so P*V stacks the V
+// hi and lo planes into one N = 128 operand: Ph [Vh | Vl] and Pl [Vh | Vl]
+// accumulate into 128 TMEM columns whose two halves are summed at the end
+// (two instructions per 16 keys instead of three N = 64 ones).
 //
-// One CTA per (image*head, 128-query tile), 192 threads:
-//   warp 0      TMA: Q once, then K / V^T tiles of 128 keys (2-stage ring)
-//   warp 1      TMEM owner + MMA issuer: S into two TMEM buffers (S_{j+1}
-//               overlaps the softmax of S_j), P*V into a third region
-//   warps 2..9  softmax: warpgroup g runs an independent online softmax over
-//               key columns [64g, 64g + 64) of every S tile (its own max, sum,
-//               P sub-tile, P*V accumulator and O registers); the two partial
-//               results are merged once at the end.  One query row per thread.
+// One CTA per (image*head, 256 queries) = two 128-query tiles A and B that
+// share every K / V tile, 320 threads:
+//   warp 0      TMA: both Q tiles once, then K / V^T tiles of 128 keys
+//               (2-stage ring)
+//   warp 1      TMEM owner + MMA issuer, ping-ponging the tiles so that the
+//               softmax of one overlaps the tensor-core work of the other:
+//                 P*V_A(j), S_A(j+1), P*V_B(j), S_B(j+1), ...
+//   warps 2..5  softmax of tile A, warps 6..9 of tile B: one query row per
+//               thread, the whole 128-key score row in registers.
+// TMEM (512 columns): S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512)
+// (O columns [0,64) accumulate P*Vh, [64,128) P*Vl).
+// The softmax overwrites its S columns with P: the 32 keys of S columns
+// [32c, 32c+32) become fp16 hi in columns [32c, 32c+16) and lo in
+// [32c+16, 32c+32), and the P*V MMA reads P straight from TMEM (A operand),
+// so P never touches shared memory.  O accumulates in TMEM across key tiles; a
+// row's running max is raised (and its O row rescaled in TMEM) only when a
+// tile's max exceeds it by more than 2^8, so P <= 256 and the rescale is rare.
+// The next S of a tile overwrites its P columns, so the MMA warp issues it
+// only after that tile's P*V has completed (waits overlap the other tile's
+// MMAs).
 // Layouts: Q, K [bh][n][64]; V^T [bh][64][vt_pitch] (keys >= n read as zero);
 // O [(img*n + q)][head*64 + d].
 #include "g4m_kernels.h"
@@ -26,30 +42,26 @@ namespace g4m {
 
 namespace {
 
-constexpr int kSoftGroups = 2;                        // softmax warpgroups (key-column halves)
-constexpr int kThreads = 64 + 128 * kSoftGroups;
-constexpr int QT = 128;                // queries per CTA
+constexpr int kThreads = 64 + 256;
+constexpr int QT = 128;                // queries per tile (two tiles per CTA)
 constexpr int KT = 128;                // keys per tile
 constexpr int HD = 64;
 constexpr int TILE_BYTES = 128 * 128;  // one [128 rows x 64 fp16] swizzled tile
-constexpr int Q_OFF = 0;                         // q hi, q lo
-constexpr int KV_OFF = 2 * TILE_BYTES;           // 2 stages x (k hi, k lo, vt hi (2 x 8K), vt lo (2 x 8K))
+constexpr int Q_OFF = 0;               // tile t: q hi at 2t, q lo at 2t+1 (x TILE_BYTES)
+constexpr int KV_OFF = 4 * TILE_BYTES; // 2 stages x (k hi, k lo, [vt hi | vt lo] keys 0-63, keys 64-127)
 constexpr int KV_STAGE = 4 * TILE_BYTES;
-constexpr int P_OFF = KV_OFF + 2 * KV_STAGE;     // p hi (2 sub-tiles), p lo (2 sub-tiles)
-constexpr int SMEM_BYTES = P_OFF + 4 * TILE_BYTES;
+constexpr int SMEM_BYTES = KV_OFF + 2 * KV_STAGE;
 constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
-constexpr uint32_t TMEM_COLS = 512;  // S0 [0,128) S1 [128,256) PV0 [256,320) PV1 [320,384)
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t O_COL = 256;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescale = 8.0f;       // log2 of the largest P before a rescale
 static_assert(SMEM_ALLOC + 512 <= 232448, "dynamic + static shared memory exceeds 227 KB per block");
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t* r) {
@@ -64,12 +76,50 @@ __device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t* r) {
       : "r"(taddr));
 }
 
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 
-// Byte offset of element (row, col) of a [rows x 64] fp16 tile in the
-// 128-byte swizzle layout (16-byte chunk index XOR row % 8).
-__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
-  return (uint32_t)row * 128u + ((uint32_t)(((col >> 3) ^ (row & 7)) << 4)) + (uint32_t)((col & 7) << 1);
+// Thread i of the warp writes lane (lane_base + i), columns [col, col+16).
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16: A is M=128 rows in TMEM lanes,
+// two fp16 K-elements per 32-bit column.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Bounded wait that ignores the CTA abort flag (exit-path drains).
+__device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t b = smem_u32(bar);
+  const long long t0 = clock64();
+  while (!mbar_try_wait(b, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, kErrWaitDrain);
+      return;
+    }
+  }
 }
 
 }  // namespace
@@ -80,13 +130,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap mVh, const __grid_constant__ CUtensorMap mVl, int n, int heads,
                    __half* __restrict__ o_hi, __half* __restrict__ o_lo, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t b_q, b_kvf[2], b_kve[2], b_sf[2], b_se[2], b_p, b_pv;
+  __shared__ __align__(8) uint64_t b_q, b_kvf[2], b_kve[2], b_s[2], b_p[2], b_pv[2], b_done;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag, skip;
 
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bh = blockIdx.y, q0 = blockIdx.x * QT;
+  const int bh = blockIdx.y, q0 = blockIdx.x * 2 * QT;
   const int T = (n + KT - 1) / KT;
 
   if (threadIdx.x == 0) {
@@ -96,11 +146,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < 2; ++s) {
       mbar_init(&b_kvf[s], 1);
       mbar_init(&b_kve[s], 1);
-      mbar_init(&b_sf[s], 1);
-      mbar_init(&b_se[s], 4 * kSoftGroups);
+      mbar_init(&b_s[s], 1);
+      mbar_init(&b_p[s], 4);
+      mbar_init(&b_pv[s], 1);
     }
-    mbar_init(&b_p, 4 * kSoftGroups);
-    mbar_init(&b_pv, 1);
+    mbar_init(&b_done, 1);
     fence_mbar_init();
   }
   __syncthreads();
@@ -116,9 +166,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tmap(&mQh);
       prefetch_tmap(&mKh);
       prefetch_tmap(&mVh);
-      mbar_expect_tx(&b_q, 2 * TILE_BYTES);
-      tma_load_2d(sm + Q_OFF, &mQh, &b_q, 0, bh * n + q0);
-      tma_load_2d(sm + Q_OFF + TILE_BYTES, &mQl, &b_q, 0, bh * n + q0);
+      mbar_expect_tx(&b_q, 4 * TILE_BYTES);
+      for (int t = 0; t < 2; ++t) {
+        tma_load_2d(sm + Q_OFF + 2 * t * TILE_BYTES, &mQh, &b_q, 0, bh * n + q0 + t * QT);
+        tma_load_2d(sm + Q_OFF + (2 * t + 1) * TILE_BYTES, &mQl, &b_q, 0, bh * n + q0 + t * QT);
+      }
       int issued = 0;
       for (int j = 0; j < T; ++j) {
         const int s = j & 1, k = j >> 1;
@@ -127,43 +179,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_expect_tx(&b_kvf[s], KV_STAGE);
         tma_load_2d(st, &mKh, &b_kvf[s], 0, bh * n + j * KT);
         tma_load_2d(st + TILE_BYTES, &mKl, &b_kvf[s], 0, bh * n + j * KT);
-        // V^T [64 d][128 keys] as two [64 x 64] swizzled sub-tiles per plane
-        tma_load_2d(st + 2 * TILE_BYTES, &mVh, &b_kvf[s], j * KT, bh * HD);
-        tma_load_2d(st + 2 * TILE_BYTES + TILE_BYTES / 2, &mVh, &b_kvf[s], j * KT + 64, bh * HD);
-        tma_load_2d(st + 3 * TILE_BYTES, &mVl, &b_kvf[s], j * KT, bh * HD);
-        tma_load_2d(st + 3 * TILE_BYTES + TILE_BYTES / 2, &mVl, &b_kvf[s], j * KT + 64, bh * HD);
+        // V^T [64 d][128 keys]: per 64-key half, the hi plane's 64 rows then
+        // the lo plane's, one [128 x 64] swizzled N = 128 operand
+        for (int h = 0; h < 2; ++h) {
+          tma_load_2d(st + (2 + h) * TILE_BYTES, &mVh, &b_kvf[s], j * KT + 64 * h, bh * HD);
+          tma_load_2d(st + (2 + h) * TILE_BYTES + TILE_BYTES / 2, &mVl, &b_kvf[s], j * KT + 64 * h, bh * HD);
+        }
         ++issued;
       }
       // drain: Q and the last use of each stage
-      const uint32_t qb = smem_u32(&b_q);
-      long long t0 = clock64();
-      while (!mbar_try_wait(qb, 0) && clock64() - t0 < kWaitCycles) {
-      }
-      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) {
-        const uint32_t b = smem_u32(&b_kvf[j & 1]);
-        t0 = clock64();
-        while (!mbar_try_wait(b, (j >> 1) & 1)) {
-          if (clock64() - t0 > kWaitCycles) {
-            atomicCAS(err, 0, kErrWaitDrain);
-            break;
-          }
-        }
-      }
+      drain_wait(&b_q, 0, err);
+      for (int j = issued > 2 ? issued - 2 : 0; j < issued; ++j) drain_wait(&b_kvf[j & 1], (j >> 1) & 1, err);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16_f32(128, KT);
-      constexpr uint32_t id_pv = idesc_f16_f32(128, HD);
-      const uint32_t qh = smem_u32(sm + Q_OFF), ql = qh + TILE_BYTES;
-      const uint32_t ph = smem_u32(sm + P_OFF), pl = ph + 2 * TILE_BYTES;
+      constexpr uint32_t id_pv = idesc_f16_f32(128, 2 * HD);
       bool ok = mbar_wait(&b_q, 0, err, kErrWaitFull, &abort_flag);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j & 1, k = j >> 1;
-        if (!mbar_wait(&b_kvf[s], k & 1, err, kErrWaitFull, &abort_flag)) return false;
-        if (!mbar_wait(&b_se[s], (k & 1) ^ 1, err, kErrWaitAccEmpty, &abort_flag)) return false;
+      // S_t(j) = Q_t K_j^T into TMEM columns [128 t, 128 t + 128)
+      auto issue_s = [&](int t, int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&b_kvf[s], (j >> 1) & 1, err, kErrWaitFull, &abort_flag)) return false;
         tc_fence_after();
+        const uint32_t qh = smem_u32(sm + Q_OFF + 2 * t * TILE_BYTES), ql = qh + TILE_BYTES;
         const uint32_t kh = smem_u32(sm + KV_OFF + s * KV_STAGE), kl = kh + TILE_BYTES;
-        const uint32_t d = tmem + s * KT;
+        const uint32_t d = tmem + t * KT;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const uint64_t dq = desc_k_sw128(qh + kk * 32), dk = desc_k_sw128(kh + kk * 32);
@@ -171,201 +211,167 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_f16_ss(d, dq, desc_k_sw128(kl + kk * 32), id_s, 1u);
           mma_f16_ss(d, desc_k_sw128(ql + kk * 32), dk, id_s, 1u);
         }
-        mma_commit(&b_sf[s]);
+        mma_commit(&b_s[t]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < T && ok; ++j) {
-        if (j + 1 < T && !issue_s(j + 1)) break;
-        if (!mbar_wait(&b_p, j & 1, err, kErrWaitFull, &abort_flag)) break;
+      // O_t += P_t(j) V_j with P_t in TMEM: keys [16 kk, 16 kk + 16) hi at S column
+      // 32 (kk / 2) + 8 (kk % 2), lo 16 columns further
+      auto issue_pv = [&](int t, int j) -> bool {
+        if (!mbar_wait(&b_p[t], j & 1, err, kErrWaitFull, &abort_flag)) return false;
         tc_fence_after();
-        const int s = j & 1;
-        const uint32_t vh = smem_u32(sm + KV_OFF + s * KV_STAGE + 2 * TILE_BYTES), vl = vh + TILE_BYTES;
-        // one K=64 P*V chain per key half, each into its own accumulator
+        const uint32_t v = smem_u32(sm + KV_OFF + (j & 1) * KV_STAGE + 2 * TILE_BYTES);
+        const uint32_t d = tmem + O_COL + t * 2 * HD, a = tmem + t * KT;
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint32_t d = tmem + 2 * KT + half * HD;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t off = kk * 32;
-            const uint64_t dph = desc_k_sw128(ph + half * TILE_BYTES + off);
-            const uint64_t dvh = desc_k_sw128(vh + half * (TILE_BYTES / 2) + off);
-            mma_f16_ss(d, dph, dvh, id_pv, kk > 0 ? 1u : 0u);
-            mma_f16_ss(d, dph, desc_k_sw128(vl + half * (TILE_BYTES / 2) + off), id_pv, 1u);
-            mma_f16_ss(d, desc_k_sw128(pl + half * TILE_BYTES + off), dvh, id_pv, 1u);
-          }
+        for (int kk = 0; kk < KT / 16; ++kk) {
+          const uint64_t dv = desc_k_sw128(v + (kk >> 2) * TILE_BYTES + (kk & 3) * 32);
+          const uint32_t ah = a + 32 * (kk >> 1) + 8 * (kk & 1);
+          mma_f16_ts(d, ah, dv, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_f16_ts(d, ah + 16, dv, id_pv, 1u);
         }
-        mma_commit(&b_pv);
-        mma_commit(&b_kve[s]);
+        mma_commit(&b_pv[t]);
+        return true;
+      };
+      if (ok) ok = issue_s(0, 0) && issue_s(1, 0);
+      for (int j = 0; j < T && ok; ++j) {
+        if (!(ok = issue_pv(0, j))) break;
+        if (j + 1 < T) {
+          // S_A(j+1) overwrites P_A(j): wait for P*V_A(j) (P*V_B(j-1) / S_B(j) keep the pipe busy)
+          if (!(ok = mbar_wait(&b_pv[0], j & 1, err, kErrWaitAccFull, &abort_flag))) break;
+          if (!(ok = issue_s(0, j + 1))) break;
+        }
+        if (!(ok = issue_pv(1, j))) break;
+        mma_commit(&b_kve[j & 1]);  // every MMA reading stage j & 1 has been issued
+        if (j + 1 < T) {
+          if (!(ok = mbar_wait(&b_pv[1], j & 1, err, kErrWaitAccFull, &abort_flag))) break;
+          if (!(ok = issue_s(1, j + 1))) break;
+        }
       }
-      // Let the last stage-release commits land before the CTA can exit.
-      if (ok && !abort_flag) {
-        for (int j = T > 2 ? T - 2 : 0; j < T; ++j)
-          if (!mbar_wait(&b_kve[j & 1], (j >> 1) & 1, err, kErrWaitDrain, &abort_flag)) break;
-      }
+      // Every MMA issued above completes before the CTA can exit.
+      mma_commit(&b_done);
+      drain_wait(&b_done, 0, err);
     }
   } else {
-    // softmax warps: group g = key half g of every tile
-    const int q = warp & 3;
-    const int g = (warp - 2) >> 2;
-    const int r = 32 * q + lane;
-    const uint32_t lane_base = (uint32_t)(32 * q) << 16;
-    constexpr int KH = KT / kSoftGroups;  // 64 keys per group
-    uint8_t* ph = sm + P_OFF + g * TILE_BYTES;  // this group's P sub-tile (hi)
-    uint8_t* pl = ph + 2 * TILE_BYTES;          // (lo)
-    const uint32_t pv_col = 2 * KT + g * HD;    // this group's P*V accumulator
-    float o[HD];
-#pragma unroll
-    for (int i = 0; i < HD; ++i) o[i] = 0.f;
-    float m = -INFINITY, l = 0.f, alpha_prev = 1.f;
+    // softmax of query tile t: one row per thread, TMEM lane quarter (warp % 4)
+    const int t = (warp - 2) >> 2;
+    const int qw = warp & 3;
+    const int r = 32 * qw + lane;
+    const uint32_t lane_base = (uint32_t)(32 * qw) << 16;
+    const uint32_t s_col = tmem + lane_base + t * KT;
+    const uint32_t o_col = tmem + lane_base + O_COL + t * 2 * HD;
+    float m = -INFINITY, l = 0.f;  // running max (log2 units) and row sum
     bool ok = true;
     for (int j = 0; j < T; ++j) {
-      const int b = j & 1, k = j >> 1;
-      ok = __all_sync(0xffffffffu, mbar_wait(&b_sf[b], k & 1, err, kErrWaitAccFull, &abort_flag));
+      ok = __all_sync(0xffffffffu, mbar_wait(&b_s[t], j & 1, err, kErrWaitAccFull, &abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const uint32_t sbase = tmem + lane_base + b * KT + g * KH;
-      const int kvalid = n - j * KT - g * KH;  // valid keys among this group's 64
-      const bool full = kvalid >= KH;
-      // pass 1: running max over this group's keys
-      float mt = -INFINITY;
+      const int kvalid = n - j * KT;  // < KT only on the last tile
+      float mp[8];                    // pass 1: eight independent max chains
+      {
+        uint32_t sr[KT];
 #pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        uint32_t sr[32];
-        tmem_ld32_nw(sbase + hb * 32, sr);
+        for (int c = 0; c < KT / 32; ++c) tmem_ld32_nw(s_col + 32 * c, sr + 32 * c);
         tmem_wait_ld();
-        if (full) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) mt = fmaxf(mt, __uint_as_float(sr[c]));
+        for (int u = 0; u < 8; ++u) mp[u] = __uint_as_float(sr[u]);  // key 0 is always valid
+        if (kvalid >= KT) {
+#pragma unroll
+          for (int c = 8; c < KT; ++c) mp[c & 7] = fmaxf(mp[c & 7], __uint_as_float(sr[c]));
         } else {
 #pragma unroll
-          for (int c = 0; c < 32; ++c)
-            if (hb * 32 + c < kvalid) mt = fmaxf(mt, __uint_as_float(sr[c]));
+          for (int c = 1; c < KT; ++c)
+            mp[c & 7] = fmaxf(mp[c & 7], c < kvalid ? __uint_as_float(sr[c]) : -INFINITY);
+          for (int u = 1; u < 8; ++u)
+            if (u >= kvalid) mp[u] = -INFINITY;
         }
       }
-      const float mn = fmaxf(m, mt);  // -inf only while this group has seen no valid key
-      const float alpha = (m == -INFINITY) ? 0.f : ex2((m - mn) * kLog2e);
-      const float mnl = (mn == -INFINITY) ? 0.f : mn * kLog2e;
-      if (j > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&b_pv, (j - 1) & 1, err, kErrWaitAccFull, &abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        uint32_t pv[32];
+      const float mt = fmaxf(fmaxf(fmaxf(mp[0], mp[1]), fmaxf(mp[2], mp[3])),
+                             fmaxf(fmaxf(mp[4], mp[5]), fmaxf(mp[6], mp[7]))) * kLog2e;
+      if (j == 0) {
+        m = mt;
+      } else {
+        const bool need = mt > m + kRescale;
+        if (__any_sync(0xffffffffu, need)) {
+          // O_t holds P*V through tile j-1: wait for it, then rescale the rows that need it
+          ok = __all_sync(0xffffffffu, mbar_wait(&b_pv[t], (j - 1) & 1, err, kErrWaitAccFull, &abort_flag));
+          if (!ok) break;
+          tc_fence_after();
+          const float alpha = need ? ex2(m - mt) : 1.0f;
 #pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          tmem_ld32_nw(tmem + lane_base + pv_col + hb * 32, pv);
-          tmem_wait_ld();
+          for (int h = 0; h < 2 * HD / 16; ++h) {
+            uint32_t ov[16];
+            tmem_ld16_nw(o_col + 16 * h, ov);
+            tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[hb * 32 + i] = fmaf(o[hb * 32 + i], alpha_prev, __uint_as_float(pv[i]));
+            for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st16(o_col + 16 * h, ov);
+          }
+          l *= alpha;
+          if (need) m = mt;
         }
       }
-      // pass 2: probabilities, row sum, P (hi / lo) into this group's swizzled sub-tile
-      float rs = 0.f;
+      // pass 2: P = 2^(s log2e - m) chunk by chunk (32 keys), the next chunk's
+      // TMEM load in flight while this one is converted; P hi / lo go back
+      // into the chunk's own columns.
+      const float mneg = -m;
+      float rp[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
+      uint32_t buf[2][32];
+      tmem_ld32_nw(s_col, buf[0]);
+      tmem_wait_ld();
 #pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        uint32_t sr[32];
-        tmem_ld32_nw(sbase + hb * 32, sr);
+      for (int c = 0; c < KT / 32; ++c) {
+        uint32_t* cur = buf[c & 1];
+        if (c + 1 < KT / 32) tmem_ld32_nw(s_col + 32 * (c + 1), buf[(c + 1) & 1]);
+        const int lim = kvalid - 32 * c;  // keys of this chunk that are valid (>= 32: all)
+        uint32_t hv[16], lv[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          float p0 = ex2(fmaf(__uint_as_float(cur[2 * u]), kLog2e, mneg));
+          float p1 = ex2(fmaf(__uint_as_float(cur[2 * u + 1]), kLog2e, mneg));
+          if (lim < 32) {
+            p0 = 2 * u < lim ? p0 : 0.f;
+            p1 = 2 * u + 1 < lim ? p1 : 0.f;
+          }
+          rp[u & 3] += p0 + p1;
+          split2_f16(p0, p1, hv[u], lv[u]);
+        }
+        tmem_st16(s_col + 32 * c, hv);
+        tmem_st16(s_col + 32 * c + 16, lv);
+        if (c + 1 < KT / 32) tmem_wait_ld();
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&b_p[t]);
+      l += (rp[0] + rp[1]) + (rp[2] + rp[3]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&b_pv[t], (T - 1) & 1, err, kErrWaitAccFull, &abort_flag));
+    if (ok) {
+      tc_fence_after();
+      const float inv = 1.0f / l;
+      const int qrow = q0 + t * QT + r;
+      const int img = bh / heads, head = bh % heads;
+      const size_t orow = (size_t)img * n + qrow;
+      __half* dh = o_hi + orow * (size_t)(heads * HD) + head * HD;
+      __half* dl = o_lo + orow * (size_t)(heads * HD) + head * HD;
+#pragma unroll 1
+      for (int h = 0; h < HD / 16; ++h) {
+        uint32_t ov[16], ol[16];
+        tmem_ld16_nw(o_col + 16 * h, ov);       // P * Vh
+        tmem_ld16_nw(o_col + HD + 16 * h, ol);  // P * Vl
         tmem_wait_ld();
-        if (full) {
+        if (qrow < n) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float p = ex2(fmaf(__uint_as_float(sr[c]), kLog2e, -mnl));
-            sr[c] = __float_as_uint(p);
-            rs += p;
+          for (int i = 0; i < 16; i += 8) {
+            uint32_t hv[4], lv[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int c0 = i + 2 * u, c1 = c0 + 1;
+              split2_f16((__uint_as_float(ov[c0]) + __uint_as_float(ol[c0])) * inv,
+                         (__uint_as_float(ov[c1]) + __uint_as_float(ol[c1])) * inv, hv[u], lv[u]);
+            }
+            *reinterpret_cast<uint4*>(dh + 16 * h + i) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+            *reinterpret_cast<uint4*>(dl + 16 * h + i) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
           }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float p = (hb * 32 + c < kvalid) ? ex2(fmaf(__uint_as_float(sr[c]), kLog2e, -mnl)) : 0.f;
-            sr[c] = __float_as_uint(p);
-            rs += p;
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 32; c += 8) {
-          uint32_t hv[4], lv[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            split2_f16(__uint_as_float(sr[c + 2 * u]), __uint_as_float(sr[c + 2 * u + 1]), hv[u], lv[u]);
-          const uint32_t off = sw128_off(r, hb * 32 + c);
-          *reinterpret_cast<uint4*>(ph + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-          *reinterpret_cast<uint4*>(pl + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&b_se[b]);  // S buffer b may be overwritten (tile j + 2)
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&b_p);
-      l = fmaf(l, alpha, rs);
-      alpha_prev = alpha;
-      m = mn;
-    }
-    if (ok) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&b_pv, (T - 1) & 1, err, kErrWaitAccFull, &abort_flag));
-      if (ok) {
-        tc_fence_after();
-        uint32_t pv[32];
-#pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          tmem_ld32_nw(tmem + lane_base + pv_col + hb * 32, pv);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[hb * 32 + i] = fmaf(o[hb * 32 + i], alpha_prev, __uint_as_float(pv[i]));
-        }
-      }
-    }
-    // Merge the two key halves (flash-decoding style): group g keeps output
-    // columns [32g, 32g + 32) and receives the partner's (m, l, O) for them
-    // through the P region, idle once the last P*V has completed.
-    float* xch = reinterpret_cast<float*>(sm + P_OFF);  // [group][row][34]
-    {
-      float* mine = xch + ((size_t)g * 128 + r) * 34;
-      mine[0] = m;
-      mine[1] = l;
-      if (g == 0) {  // hand the partner the columns it keeps (constant indices)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mine[2 + i] = o[32 + i];
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mine[2 + i] = o[i];
-      }
-    }
-    asm volatile("bar.sync %0, %1;" ::"r"(1 + q), "r"(32 * kSoftGroups) : "memory");
-    if (ok) {
-      const float* other = xch + ((size_t)(1 - g) * 128 + r) * 34;
-      const float m2 = other[0], l2 = other[1];
-      const float mm = fmaxf(m, m2);
-      const float a1 = (m == -INFINITY) ? 0.f : ex2((m - mm) * kLog2e);
-      const float a2 = (m2 == -INFINITY) ? 0.f : ex2((m2 - mm) * kLog2e);
-      const float inv = 1.0f / (l * a1 + l2 * a2);
-      float own[32];
-      if (g == 0) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) own[i] = o[i];
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) own[i] = o[32 + i];
-      }
-      const int qrow = q0 + r;
-      if (qrow < n) {
-        const int img = bh / heads, head = bh % heads;
-        const size_t orow = (size_t)img * n + qrow;
-        __half* dh = o_hi + orow * (size_t)(heads * HD) + head * HD + 32 * g;
-        __half* dl = o_lo + orow * (size_t)(heads * HD) + head * HD + 32 * g;
-#pragma unroll
-        for (int i = 0; i < 32; i += 8) {
-          uint32_t hv[4], lv[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float v0 = (own[i + 2 * u] * a1 + other[2 + i + 2 * u] * a2) * inv;
-            const float v1 = (own[i + 2 * u + 1] * a1 + other[2 + i + 2 * u + 1] * a2) * inv;
-            split2_f16(v0, v1, hv[u], lv[u]);
-          }
-          *reinterpret_cast<uint4*>(dh + i) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-          *reinterpret_cast<uint4*>(dl + i) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
         }
       }
     }
@@ -401,7 +407,7 @@ cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __
   if (!make_tmap_f16_any(&mVh, vt_hi, (uint64_t)bh * HD, (uint64_t)n, (uint64_t)vt_pitch, 64) ||
       !make_tmap_f16_any(&mVl, vt_lo, (uint64_t)bh * HD, (uint64_t)n, (uint64_t)vt_pitch, 64))
     return cudaErrorInvalidValue;
-  dim3 grid((n + QT - 1) / QT, bh);
+  dim3 grid((n + 2 * QT - 1) / (2 * QT), bh);
   attn_tc_kernel<<<grid, kThreads, SMEM_ALLOC, st>>>(mQh, mQl, mKh, mKl, mVh, mVl, n, heads, o_hi, o_lo, err);
   return cudaGetLastError();
 }
