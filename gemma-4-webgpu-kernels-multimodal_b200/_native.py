@@ -222,7 +222,7 @@ class Context:
         return [o[: int(r)] for o, r in zip(outs, rows)], rows
 
     def audio_debug_hidden(self, rows: int, which: int = 1, device=0) -> np.ndarray:
-        out = np.empty((rows, 1024), np.float32)
+        out = np.empty((rows, 3072 if which == 2 else 1024), np.float32)
         check(lib().g4m_audio_debug_hidden(self.h, device, which, ptr(out), out.size))
         return out
 

@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap mQh, const __grid_constant__ CUtensorMap mQl,
                    const __grid_constant__ CUtensorMap mKh, const __grid_constant__ CUtensorMap mKl,
                    const __grid_constant__ CUtensorMap mVh, const __grid_constant__ CUtensorMap mVl, int n, int heads,
-                   __half* __restrict__ o_hi, __half* __restrict__ o_lo, int* err) {
+                   __half* __restrict__ o_hi, __half* __restrict__ o_lo, float s_code, int* err) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t b_q, b_kvf[2], b_kve[2], b_s[2], b_p[2], b_pv[2], b_done;
   __shared__ uint32_t tmem_slot;
@@ -366,11 +366,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const int c0 = i + 2 * u, c1 = c0 + 1;
-              split2_f16((__uint_as_float(ov[c0]) + __uint_as_float(ol[c0])) * inv,
-                         (__uint_as_float(ov[c1]) + __uint_as_float(ol[c1])) * inv, hv[u], lv[u]);
+              const float x0 = (__uint_as_float(ov[c0]) + __uint_as_float(ol[c0])) * inv;
+              const float x1 = (__uint_as_float(ov[c1]) + __uint_as_float(ol[c1])) * inv;
+              if (s_code != 0.0f) {  // integer codes for the o_proj input scale
+                union {
+                  __half2 h2;
+                  uint32_t w;
+                } cv;
+                cv.h2 = __floats2half2_rn(srq_code(x0, s_code), srq_code(x1, s_code));
+                hv[u] = cv.w;
+              } else {
+                split2_f16(x0, x1, hv[u], lv[u]);
+              }
             }
             *reinterpret_cast<uint4*>(dh + 16 * h + i) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-            *reinterpret_cast<uint4*>(dl + 16 * h + i) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            if (s_code == 0.0f) *reinterpret_cast<uint4*>(dl + 16 * h + i) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
           }
         }
       }
@@ -387,7 +397,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
                                 const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
-                                __half* o_hi, __half* o_lo, int* err, cudaStream_t st) {
+                                __half* o_hi, __half* o_lo, float s_code, int* err, cudaStream_t st) {
   if (bh <= 0 || n <= 0) return cudaSuccess;
   if (vt_pitch % 64 != 0 || vt_pitch < n) return cudaErrorInvalidValue;
   static bool attr[64] = {false};
@@ -408,7 +418,7 @@ cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __
       !make_tmap_f16_any(&mVl, vt_lo, (uint64_t)bh * HD, (uint64_t)n, (uint64_t)vt_pitch, 64))
     return cudaErrorInvalidValue;
   dim3 grid((n + 2 * QT - 1) / (2 * QT), bh);
-  attn_tc_kernel<<<grid, kThreads, SMEM_ALLOC, st>>>(mQh, mQl, mKh, mKl, mVh, mVl, n, heads, o_hi, o_lo, err);
+  attn_tc_kernel<<<grid, kThreads, SMEM_ALLOC, st>>>(mQh, mQl, mKh, mKl, mVh, mVl, n, heads, o_hi, o_lo, s_code, err);
   return cudaGetLastError();
 }
 

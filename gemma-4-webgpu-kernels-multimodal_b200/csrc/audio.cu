@@ -323,17 +323,14 @@ ClipShape clip_shape(long n) {
     if (e_ != cudaSuccess) return fail(G4M_E_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
   } while (0)
 
+// q / k / v share one operand: all three use static input quantisation or
+// none of them; every other linear is independent.
 static int audio_check_quant(const AudioWeights& aw, int layers) {
-  for (int i = 0; i < layers; ++i) {
-    const AudioLayer& L = aw.L[i];
-    const float s[] = {L.sin_ff[0][0], L.sin_ff[0][1], L.sin_ff[1][0], L.sin_ff[1][1], L.sin_qkv[0], L.sin_qkv[1],
-                       L.sin_qkv[2], L.sin_post, L.sin_start, L.sin_end};
-    for (float v : s)
-      if (v != 0)
-        return fail(G4M_E_UNSUPPORTED, "audio layer " + std::to_string(i) +
-                                           ": static input-activation quantisation (input_activation_scale != 0) is "
-                                           "not supported by the fused tower path");
-  }
+  for (int i = 0; i < layers; ++i)
+    if (quant_group(aw.L[i].sin_qkv, 3) < 0)
+      return fail(G4M_E_UNSUPPORTED, "audio layer " + std::to_string(i) +
+                                         ": q/k/v projections mix zero and non-zero input_activation_scale; they "
+                                         "share one operand");
   return G4M_OK;
 }
 
@@ -344,9 +341,20 @@ static GemmArgs aargs(Device& d, long M, int N, int K) {
   a.N = N;
   a.K = K;
   a.row_scale = 1.0f;
+  a.row_scale_b = 1.0f;
+  a.row_scale_c = 1.0f;
   a.eps = 1e-6f;
   a.err = d.err;
   return a;
+}
+
+// Next-operand fields of a row pass whose consumers have input scales s[0..n)
+// (integer code planes a_hi, a_lo, a_c when they are non-zero).
+static void next_scales(RowArgs& r, const float* s, int n, __half* a_c) {
+  r.s_in_next = s ? s[0] : 0.0f;
+  r.s_in_b = (s && n > 1) ? s[1] : 0.0f;
+  r.s_in_c = (s && n > 2) ? s[2] : 0.0f;
+  r.a_c = (s && n > 2 && s[0] != 0.0f) ? a_c : nullptr;
 }
 
 // Row metadata of a packed batch: clip of every row, first row and row count
@@ -373,6 +381,10 @@ static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out
       ensure(b.y, M * D * 4) || ensure(b.qkv, M * 3 * D * 4) || ensure(b.g, M * D * 4) || ensure(b.a_hi, M * D * 2) ||
       ensure(b.a_lo, M * D * 2) || ensure(b.f_hi, M * FF * 2) || ensure(b.f_lo, M * FF * 2) ||
       ensure(b.proj, M * OUT * 4) || ensure(b.e_hi, M * OUT * 2) || ensure(b.e_lo, M * OUT * 2))
+    return fail(G4M_E_CUDA, "audio activation allocation failed (" + std::to_string(M) + " rows)");
+  bool codes3 = false;  // a third code plane for layers with quantised q / k / v
+  for (int i = 0; i < d.aw.layers; ++i) codes3 = codes3 || d.aw.L[i].sin_qkv[0] != 0.0f;
+  if (codes3 && ensure(b.a_c, M * D * 2))
     return fail(G4M_E_CUDA, "audio activation allocation failed (" + std::to_string(M) + " rows)");
   G4M_LAUNCH_A(cudaMemcpyAsync(b.clip_row0.p, row0.data(), n * 4, cudaMemcpyHostToDevice, st));
   G4M_LAUNCH_A(cudaMemcpyAsync(b.clip_rows.p, rows.data(), n * 4, cudaMemcpyHostToDevice, st));
@@ -409,22 +421,30 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
   GemmArgs a;
   GemmOperands op;
   int rc = G4M_OK;
-  auto ffn = [&](const AudioLayer& L, int blk, const float* w_next, const float* w_out) -> int {
+  __half* ac = (__half*)b.a_c.p;
+  // Feed-forward block `blk`; its final row pass also produces the operand
+  // of the next linear (norm w_next, input scales s_next[0..n_next)).
+  auto ffn = [&](const AudioLayer& L, int blk, const float* w_next, const float* s_next, int n_next,
+                 const float* w_out) -> int {
+    const float s1 = L.sin_ff[blk][0], s2 = L.sin_ff[blk][1];
     GemmArgs g = aargs(d, M, FF, D);
     g.col_scale = L.s_ff1[blk];
     g.s_out = L.sout_ff[blk][0];
     g.out_hi = (__half*)b.f_hi.p;
     g.out_lo = (__half*)b.f_lo.p;
     g.ldh = FF;
+    g.s_code = s2;  // ffw_layer_2's input scale: store codes
+    if (s1 != 0.0f) g.row_scale = s1;
     GemmOperands o{ah, al, L.w_ff1[blk], nullptr};
-    G4M_RUN("gemm_ffw1", gemm_launch(256, 2, EPI_SILU, o, g, st));
+    G4M_RUN("gemm_ffw1", gemm_launch(256, s1 != 0.0f ? 1 : 2, EPI_SILU, o, g, st));
     g = aargs(d, M, D, FF);
     g.col_scale = L.s_ff2[blk];
     g.s_out = L.sout_ff[blk][1];
     g.out_f32 = y;
     g.ldo = D;
+    if (s2 != 0.0f) g.row_scale = s2;
     o = GemmOperands{(const __half*)b.f_hi.p, (const __half*)b.f_lo.p, L.w_ff2[blk], nullptr};
-    G4M_RUN("gemm_ffw2", gemm_launch(256, 2, EPI_F32, o, g, st));
+    G4M_RUN("gemm_ffw2", gemm_launch(256, s2 != 0.0f ? 1 : 2, EPI_F32, o, g, st));
     RowArgs q = r;
     q.h_in = h;
     q.h_out = h;
@@ -433,34 +453,44 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
     q.res_scale = 0.5f;  // AUDIO_FEED_FORWARD_RESIDUAL_WEIGHT, src/model.ts:91
     q.w_out = w_out;
     q.w_next = w_next;
+    next_scales(q, s_next, n_next, ac);
     G4M_RUN("rows", fused_rows(q, st));
     return G4M_OK;
   };
   for (int i = first; i < first + count; ++i) {
     if (ctx->cancel.load()) return fail(G4M_E_CANCELLED, "Aborted");
     const AudioLayer& L = aw.L[i];
-    if ((rc = ffn(L, 0, L.n_pre_attn, nullptr))) return rc;
+    if ((rc = ffn(L, 0, L.n_pre_attn, L.sin_qkv, 3, nullptr))) return rc;
     // self attention (src/audio/encoder.ts:1011-1071)
+    const bool qkv_codes = L.sin_qkv[0] != 0.0f;  // all-zero or all-non-zero (audio_check_quant)
     a = aargs(d, M, 3 * D, D);
     a.col_scale = L.sqkv;
+    if (qkv_codes) {
+      a.row_scale = L.sin_qkv[0];
+      a.row_scale_b = L.sin_qkv[1];
+      a.row_scale_c = L.sin_qkv[2];
+    }
     a.proj_width = D;
     a.s_out = L.sout_qkv[0];
     a.s_out_b = L.sout_qkv[1];
     a.s_out_c = L.sout_qkv[2];
     a.out_f32 = (float*)b.qkv.p;
     a.ldo = 3 * D;
-    op = GemmOperands{ah, al, L.wqkv, nullptr};
-    G4M_RUN("gemm_qkv", gemm_launch(256, 2, EPI_F32, op, a, st));
+    op = GemmOperands{ah, al, L.wqkv, nullptr, ac};
+    if (qkv_codes) G4M_RUN("gemm_qkv", gemm_launch(256, 1, EPI_F32, op, a, st, 0, 1));
+    else G4M_RUN("gemm_qkv", gemm_launch(256, 2, EPI_F32, op, a, st));
     G4M_RUN("attention", audio_attention_blocks((const float*)b.qkv.p, L.relk, L.pds, (const int*)b.t1_off.p,
                                                 (const int*)b.t1_len.p, nblocks, drow0, drows,
-                                                (float)(log(1.0 + exp(1.0)) / log(2.0)), 50.0f, ah, al, st));
+                                                (float)(log(1.0 + exp(1.0)) / log(2.0)), 50.0f, ah, al, L.sin_post,
+                                                st));
     a = aargs(d, M, D, D);
     a.col_scale = L.spost;
     a.s_out = L.sout_post;
     a.out_f32 = y;
     a.ldo = D;
+    if (L.sin_post != 0.0f) a.row_scale = L.sin_post;
     op = GemmOperands{ah, al, L.wpost, nullptr};
-    G4M_RUN("gemm_post", gemm_launch(256, 2, EPI_F32, op, a, st));
+    G4M_RUN("gemm_post", gemm_launch(256, L.sin_post != 0.0f ? 1 : 2, EPI_F32, op, a, st));
     RowArgs q = r;
     q.y = y;
     q.w_post = L.n_post_attn;
@@ -468,6 +498,7 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
     q.h_in = h;
     q.h_out = h;
     q.w_next = L.n_lpre;
+    next_scales(q, &L.sin_start, 1, nullptr);
     G4M_RUN("rows", fused_rows(q, st));
     // light conv (src/audio/encoder.ts:923-1009)
     a = aargs(d, M, 2 * D, D);
@@ -476,16 +507,19 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
     a.s_out_b = L.sout_start[1];
     a.out_f32 = (float*)b.g.p;
     a.ldo = D;
+    if (L.sin_start != 0.0f) a.row_scale = a.row_scale_b = L.sin_start;
     op = GemmOperands{ah, al, L.wstart, nullptr};
-    G4M_RUN("gemm_lconv_start", gemm_launch(256, 2, EPI_GLU, op, a, st));
-    G4M_RUN("lconv", audio_lconv_rows((const float*)b.g.p, L.dw, L.n_conv, drc, drow0, M, 1e-6f, ah, al, st));
+    G4M_RUN("gemm_lconv_start", gemm_launch(256, L.sin_start != 0.0f ? 1 : 2, EPI_GLU, op, a, st));
+    G4M_RUN("lconv",
+            audio_lconv_rows((const float*)b.g.p, L.dw, L.n_conv, drc, drow0, M, 1e-6f, ah, al, L.sin_end, st));
     a = aargs(d, M, D, D);
     a.col_scale = L.send;
     a.s_out = L.sout_end;
     a.out_f32 = y;
     a.ldo = D;
+    if (L.sin_end != 0.0f) a.row_scale = L.sin_end;
     op = GemmOperands{ah, al, L.wend, nullptr};
-    G4M_RUN("gemm_lconv_end", gemm_launch(256, 2, EPI_F32, op, a, st));
+    G4M_RUN("gemm_lconv_end", gemm_launch(256, L.sin_end != 0.0f ? 1 : 2, EPI_F32, op, a, st));
     q = r;
     q.y = y;
     q.w_post = nullptr;
@@ -493,9 +527,12 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
     q.h_in = h;
     q.h_out = h;
     q.w_next = L.n_ff_pre[1];
+    next_scales(q, &L.sin_ff[1][0], 1, nullptr);
     G4M_RUN("rows", fused_rows(q, st));
     const bool more = i + 1 < first + count || (next_operand && i + 1 < aw.layers);
-    if ((rc = ffn(L, 1, more ? aw.L[i + 1].n_ff_pre[0] : nullptr, L.n_out))) return rc;
+    if ((rc = ffn(L, 1, more ? aw.L[i + 1].n_ff_pre[0] : nullptr, more ? &aw.L[i + 1].sin_ff[0][0] : nullptr, 1,
+                  L.n_out)))
+      return rc;
   }
   return G4M_OK;
 }
@@ -566,6 +603,7 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   r.eps = 1e-6f;
   r.h_in = h;
   r.w_next = aw.L[0].n_ff_pre[0];
+  next_scales(r, &aw.L[0].sin_ff[0][0], 1, nullptr);
   r.a_hi = ah;
   r.a_lo = al;
   r.lda = D;
@@ -611,6 +649,7 @@ int audio_layers_host(g4m_ctx* ctx, Device& d, const std::vector<int>& rows, int
   r.eps = 1e-6f;
   r.h_in = (const float*)b.h.p;
   r.w_next = aw.L[first].n_ff_pre[0];
+  next_scales(r, &aw.L[first].sin_ff[0][0], 1, nullptr);
   r.a_hi = (__half*)b.a_hi.p;
   r.a_lo = (__half*)b.a_lo.p;
   r.lda = D;
@@ -750,8 +789,9 @@ int g4m_audio_debug_hidden(g4m_ctx* ctx, int di, int which, float* host, size_t 
   Device& d = *ctx->devs[di];
   std::lock_guard<std::mutex> lk(d.mu);
   cudaSetDevice(d.id);
-  const size_t need_n = (size_t)d.last_audio_rows * 1024;
-  const DevBuf& src = which == 0 ? d.ab.h0 : d.ab.h;
+  if (which < 0 || which > 2) return fail(G4M_E_ARG, "which must be 0, 1 or 2");
+  const size_t need_n = (size_t)d.last_audio_rows * (which == 2 ? 3 * 1024 : 1024);
+  const DevBuf& src = which == 0 ? d.ab.h0 : (which == 1 ? d.ab.h : d.ab.qkv);
   if (!src.p || need_n == 0) return fail(G4M_E_ARG, "no audio stage output is available");
   if (count < need_n) return fail(G4M_E_ARG, "host buffer too small");
   if (cudaDeviceSynchronize() || cudaMemcpy(host, src.p, need_n * 4, cudaMemcpyDeviceToHost))

@@ -8,6 +8,15 @@
 
 namespace g4m {
 
+// srqScalar's integer code (src/kernels/qat.ts:489-492): clamp(round(v / s),
+// -128, 127) with JS Math.round (ties toward +inf).
+__device__ __forceinline__ float srq_code(float v, float s) {
+  const float q = __fdiv_rn(v, s);
+  const float f = floorf(q);
+  const float r = (q - f >= 0.5f) ? f + 1.0f : f;
+  return fminf(fmaxf(r, -128.0f), 127.0f);
+}
+
 enum Epi : int {
   EPI_F32 = 0,         // y = srq(acc * row_scale * col_scale[n], s_out) (+ bias[n]) -> f32
   EPI_GELU_GATE = 2,   // tile halves (gate | up) -> gelu_tanh(gate) * up -> fp16 hi/lo
@@ -17,17 +26,32 @@ enum Epi : int {
   EPI_PATCH = 6,       // acc + pos_x row + pos_y row -> f32
 };
 
+// Static input-activation quantisation (input_activation_scale s != 0,
+// srqScalar in src/kernels/qat.ts:489-492): an operand producer stores the
+// integer code clamp(round(x / s), -128, 127) (exact in fp16) in place of the
+// hi/lo split, the GEMM runs one term on the codes and its epilogue scales by
+// s.  Projections that share an input (q / k / v, gate / up) keep their own
+// s, so their GEMM selects the code plane per output region (amode):
+//   amode 0  one A for the whole GEMM (terms 1..3 as above)
+//   amode 1  one code plane per proj_width-column region, chosen per tile
+//            (a_hi region 0, a_lo region 1, a_c region 2)
+//   amode 2  tile halves: columns [0, BN/2) use a_hi, [BN/2, BN) a_lo (the
+//            interleaved gate | up layout)
 struct GemmOperands {
   const __half* a_hi;  // [M, K]
-  const __half* a_lo;  // [M, K] (terms >= 2)
+  const __half* a_lo;  // [M, K] (terms >= 2; amode 1/2: the second code plane)
   const __half* b_hi;  // [N, K]
   const __half* b_lo;  // [N, K] (terms == 3)
+  const __half* a_c;   // [M, K] amode 1: the third code plane
 };
 
 struct GemmArgs {
   int M, N, K;
   const float* col_scale;  // [N] per-output-channel weight scale (may be null for EPI_F32)
   float row_scale;         // 1, or s_in when A holds integer codes
+  float row_scale_b;       // amode 1/2: s_in of region / half 1 (else = row_scale)
+  float row_scale_c;       // amode 1: s_in of region 2
+  float s_code;            // EPI_GELU_GATE / EPI_SILU: store codes for the next GEMM's s_in (0: hi/lo)
   float s_out, s_out_b, s_out_c;
   const float* bias;       // [N] or null
   float* out_f32;
@@ -53,7 +77,7 @@ struct GemmArgs {
 };
 
 cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args, cudaStream_t st,
-                        int max_ctas = 0);
+                        int max_ctas = 0, int amode = 0);
 bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 // Any cols with a 16-byte-multiple row pitch `pitch_elems` (>= cols).
 bool make_tmap_f16_any(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
@@ -78,9 +102,11 @@ struct RowArgs {
   const float* w_out;      // optional RMSNorm of the new residual (audio norm_out)
   float* h_out;            // residual output (may alias h_in)
   const float* w_next;     // optional RMSNorm producing the next GEMM operand
-  float s_in_next;         // srq of the next operand (0 = identity)
+  float s_in_next;         // 0: hi/lo planes.  Else integer codes for s_in_next in a_hi,
+  float s_in_b, s_in_c;    // and (when non-zero) codes for s_in_b in a_lo, for s_in_c in a_c
   __half* a_hi;
   __half* a_lo;
+  __half* a_c;
   long lda;
 };
 cudaError_t fused_rows(const RowArgs& r, cudaStream_t st);
@@ -90,12 +116,13 @@ cudaError_t vision_patch_operand(const float* pixels, int n_images, int height, 
                                  __half* lo, cudaStream_t st);
 cudaError_t vision_pool_operand(const float* h, const int* pool_idx, int n_images, int rows_per_image, int tokens,
                                 int k2, int d, float eps, float* pooled_out, __half* hi, __half* lo, cudaStream_t st);
+// s_code != 0: O is stored as integer codes for the o_proj input scale (o_hi only).
 cudaError_t vision_attention_simt(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
                                   const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
-                                  __half* o_hi, __half* o_lo, cudaStream_t st);
+                                  __half* o_hi, __half* o_lo, float s_code, cudaStream_t st);
 cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
                                 const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
-                                __half* o_hi, __half* o_lo, int* err, cudaStream_t st);
+                                __half* o_hi, __half* o_lo, float s_code, int* err, cudaStream_t st);
 
 // Audio helpers -- kernels_audio.cu
 cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
@@ -106,9 +133,9 @@ cudaError_t audio_subsample(const float* feats, const int* frame_off, const int*
                             const float* w1t, const float* n1, float eps, __half* a_hi, __half* a_lo, cudaStream_t st);
 cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
                                    const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
-                                   float softcap, __half* o_hi, __half* o_lo, cudaStream_t st);
+                                   float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st);
 cudaError_t audio_lconv_rows(const float* g, const float* dw, const float* nw, const int* row_clip, const int* row0,
-                             long rows, float eps, __half* a_hi, __half* a_lo, cudaStream_t st);
+                             long rows, float eps, __half* a_hi, __half* a_lo, float s_code, cudaStream_t st);
 cudaError_t gather_rows(const float* src, const int* rows_idx, long n, int d, float* dst, cudaStream_t st);
 cudaError_t row_inv_rms_operand(const float* x, long rows, int d, float eps, __half* hi, __half* lo, cudaStream_t st);
 cudaError_t add_bias_rows(float* y, const float* b, long rows, int d, cudaStream_t st);

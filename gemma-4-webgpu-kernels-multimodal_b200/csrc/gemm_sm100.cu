@@ -35,9 +35,9 @@ constexpr int BK = 64;
 constexpr int kEpiGroups = 2;                       // epilogue warpgroups
 constexpr int kGemmThreads = 64 + 128 * kEpiGroups;  // producer, MMA, epilogue
 
-template <int BN, int TERMS>
+template <int BN, int TERMS, int AMODE = 0>
 struct GemmCfg {
-  static constexpr int NA = TERMS >= 2 ? 2 : 1;
+  static constexpr int NA = (TERMS >= 2 || AMODE == 2) ? 2 : 1;
   static constexpr int NB = TERMS == 3 ? 2 : 1;
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
@@ -47,17 +47,10 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = 2 * BN;
 };
 
-__device__ __forceinline__ float js_round_f(float x) {
-  float f = floorf(x);
-  return (x - f >= 0.5f) ? f + 1.0f : f;
-}
-
 // srqScalar (src/kernels/qat.ts:489-492): clamp(round(v/s), -128, 127) * s.
 __device__ __forceinline__ float srq_f(float v, float s) {
   if (s == 0.0f) return v;
-  float r = js_round_f(__fdiv_rn(v, s));
-  r = fminf(fmaxf(r, -128.0f), 127.0f);
-  return r * s;
+  return srq_code(v, s) * s;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -108,11 +101,30 @@ __device__ __forceinline__ void load_scales32(const float* p, float* s) {
   }
 }
 
-template <int BN, int TERMS, int EPI>
+// Codes for the next GEMM's input scale (EPI_GELU_GATE / EPI_SILU outputs).
+__device__ __forceinline__ void store_codes_row(__half* dst, const float* v, float s, int n) {
+  for (int j = 0; j < n; j += 8) {
+    uint32_t hv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      union {
+        __half2 h;
+        uint32_t w;
+      } c;
+      c.h = __floats2half2_rn(srq_code(v[j + 2 * u], s), srq_code(v[j + 2 * u + 1], s));
+      hv[u] = c.w;
+    }
+    *reinterpret_cast<uint4*>(dst + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
+
+template <int BN, int TERMS, int EPI, int AMODE>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap mA0, const __grid_constant__ CUtensorMap mA1,
-                   const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1, GemmArgs a) {
-  using C = GemmCfg<BN, TERMS>;
+                   const __grid_constant__ CUtensorMap mB0, const __grid_constant__ CUtensorMap mB1,
+                   const __grid_constant__ CUtensorMap mA2, GemmArgs a) {
+  static_assert(AMODE == 0 || TERMS == 1, "per-region A selection runs on integer codes (one term)");
+  using C = GemmCfg<BN, TERMS, AMODE>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[C::STAGES], bar_empty[C::STAGES], bar_accf[2], bar_acce[2];
   __shared__ uint32_t tmem_slot;
@@ -141,8 +153,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&mA0);
     prefetch_tmap(&mB0);
-    if (C::NA == 2) prefetch_tmap(&mA1);
+    if (C::NA == 2 || AMODE == 1) prefetch_tmap(&mA1);
     if (C::NB == 2) prefetch_tmap(&mB1);
+    if (AMODE == 1) prefetch_tmap(&mA2);
   }
   if (warp == 1) tmem_alloc(&tmem_slot, C::TMEM_COLS);
   tc_fence_before();
@@ -168,7 +181,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           mbar_expect_tx(&bar_full[s], C::STAGE_BYTES);
-          tma_load_2d(sA(s, 0), &mA0, &bar_full[s], kb * BK, mb * BM);
+          if (AMODE == 1) {
+            const int region = nb * BN / a.proj_width;
+            const CUtensorMap* ma = region == 0 ? &mA0 : (region == 1 ? &mA1 : &mA2);
+            tma_load_2d(sA(s, 0), ma, &bar_full[s], kb * BK, mb * BM);
+          } else {
+            tma_load_2d(sA(s, 0), &mA0, &bar_full[s], kb * BK, mb * BM);
+          }
           if (C::NA == 2) tma_load_2d(sA(s, 1), &mA1, &bar_full[s], kb * BK, mb * BM);
           tma_load_2d(sB(s, 0), &mB0, &bar_full[s], kb * BK, nb * BN);
           if (C::NB == 2) tma_load_2d(sB(s, 1), &mB1, &bar_full[s], kb * BK, nb * BN);
@@ -191,6 +210,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
+      constexpr uint32_t idesc_half = idesc_f16_f32(BM, BN / 2);
       uint32_t it = 0, t = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++t) {
@@ -210,6 +230,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint64_t da0 = desc_k_sw128(a0 + k * 32), db0 = desc_k_sw128(b0 + k * 32);
+            if (AMODE == 2) {
+              // halves of the B tile (rows [0, BN/2) and [BN/2, BN)) against their own codes
+              const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+              mma_f16_ss(d, da0, db0, idesc_half, acc);
+              mma_f16_ss(d + BN / 2, desc_k_sw128(smem_u32(sA(s, 1)) + k * 32),
+                         desc_k_sw128(b0 + (BN / 2) * 128 + k * 32), idesc_half, acc);
+              continue;
+            }
             mma_f16_ss(d, da0, db0, idesc, (kb > 0 || k > 0) ? 1u : 0u);
             if (TERMS >= 2) mma_f16_ss(d, desc_k_sw128(smem_u32(sA(s, 1)) + k * 32), db0, idesc, 1u);
             if (TERMS == 3) mma_f16_ss(d, da0, desc_k_sw128(smem_u32(sB(s, 1)) + k * 32), idesc, 1u);
@@ -264,11 +292,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               // fused projections (proj_width > 0) keep their own output scales
               const int which = a.proj_width > 0 ? n0 / a.proj_width : 0;
               const float so = which == 0 ? a.s_out : (which == 1 ? a.s_out_b : a.s_out_c);
+              const float rsw = AMODE == 1 ? (which == 0 ? rs : (which == 1 ? a.row_scale_b : a.row_scale_c)) : rs;
               if (a.col_scale) {
                 float sc[32];
                 load_scales32(a.col_scale + n0, sc);
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = (v[j] * rs) * sc[j];
+                for (int j = 0; j < 32; ++j) v[j] = (v[j] * rsw) * sc[j];
               }
               if (so != 0.0f) {
 #pragma unroll
@@ -285,7 +314,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
             }
             if (EPI == EPI_SILU) {
-              store_f16x2_row(a.out_hi + (size_t)row * a.ldh + n0, a.out_lo + (size_t)row * a.ldh + n0, v, 32);
+              if (a.s_code != 0.0f) store_codes_row(a.out_hi + (size_t)row * a.ldh + n0, v, a.s_code, 32);
+              else store_f16x2_row(a.out_hi + (size_t)row * a.ldh + n0, a.out_lo + (size_t)row * a.ldh + n0, v, 32);
             } else {
               float* dst = a.out_f32 + (size_t)row * a.ldo + n0;
 #pragma unroll
@@ -308,10 +338,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float sg[32], su[32];
             load_scales32(a.col_scale + ng, sg);
             load_scales32(a.col_scale + nu, su);
+            const float rsu = AMODE == 2 ? a.row_scale_b : rs;
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
               g[j] = (g[j] * rs) * sg[j];
-              u[j] = (u[j] * rs) * su[j];
+              u[j] = (u[j] * rsu) * su[j];
             }
             if (a.s_out != 0.0f || a.s_out_b != 0.0f) {
 #pragma unroll
@@ -326,7 +357,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               else g[j] = g[j] * sigmoid_f(u[j]);                          // runGluActivationCpu
             }
             if (EPI == EPI_GELU_GATE) {
-              store_f16x2_row(a.out_hi + (size_t)row * a.ldh + no, a.out_lo + (size_t)row * a.ldh + no, g, 32);
+              if (a.s_code != 0.0f) store_codes_row(a.out_hi + (size_t)row * a.ldh + no, g, a.s_code, 32);
+              else store_f16x2_row(a.out_hi + (size_t)row * a.ldh + no, a.out_lo + (size_t)row * a.ldh + no, g, 32);
             } else {
               float* dst = a.out_f32 + (size_t)row * a.ldo + no;
 #pragma unroll
@@ -344,6 +376,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int img = valid ? row / a.rows_per_image : 0;
         const int tok = valid ? row % a.rows_per_image : 0;
         const float so = which == 0 ? a.s_out : (which == 1 ? a.s_out_b : a.s_out_c);
+        const float rsw = AMODE == 1 ? (which == 0 ? rs : (which == 1 ? a.row_scale_b : a.row_scale_c)) : rs;
         const float* nw = which == 0 ? a.qn_w : (which == 1 ? a.kn_w : nullptr);
 #pragma unroll 1
         for (int hh = eg * NH; hh < (eg + 1) * NH; ++hh) {
@@ -355,10 +388,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             float sc[32];
             load_scales32(a.col_scale + n0, sc);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = (v[j] * rs) * sc[j];
+            for (int j = 0; j < 32; ++j) v[j] = (v[j] * rsw) * sc[j];
             load_scales32(a.col_scale + n0 + 32, sc);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[32 + j] = (v[32 + j] * rs) * sc[j];
+            for (int j = 0; j < 32; ++j) v[32 + j] = (v[32 + j] * rsw) * sc[j];
             if (so != 0.0f) {
 #pragma unroll
               for (int j = 0; j < 64; ++j) v[j] = srq_f(v[j], so);
@@ -484,10 +517,10 @@ static int g_num_sms(int dev) {
   return cache[dev];
 }
 
-template <int BN, int TERMS, int EPI>
+template <int BN, int TERMS, int EPI, int AMODE>
 static cudaError_t launch_t(const GemmOperands& op, const GemmArgs& args, cudaStream_t st, int max_ctas) {
-  using C = GemmCfg<BN, TERMS>;
-  auto kern = gemm_tc_kernel<BN, TERMS, EPI>;
+  using C = GemmCfg<BN, TERMS, AMODE>;
+  auto kern = gemm_tc_kernel<BN, TERMS, EPI, AMODE>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -496,34 +529,45 @@ static cudaError_t launch_t(const GemmOperands& op, const GemmArgs& args, cudaSt
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  CUtensorMap mA0, mA1, mB0, mB1;
+  if (AMODE == 1 && (args.proj_width <= 0 || args.proj_width % BN != 0 || args.N > 3 * args.proj_width))
+    return cudaErrorInvalidValue;  // every tile must sit inside one region
+  CUtensorMap mA0, mA1, mA2, mB0, mB1;
   if (!make_tmap_f16(&mA0, op.a_hi, args.M, args.K, BM)) return cudaErrorInvalidValue;
   if (!make_tmap_f16(&mB0, op.b_hi, args.N, args.K, BN)) return cudaErrorInvalidValue;
   mA1 = mA0;
+  mA2 = mA0;
   mB1 = mB0;
-  if (C::NA == 2 && !make_tmap_f16(&mA1, op.a_lo, args.M, args.K, BM)) return cudaErrorInvalidValue;
+  if ((C::NA == 2 || AMODE == 1) && !make_tmap_f16(&mA1, op.a_lo, args.M, args.K, BM)) return cudaErrorInvalidValue;
+  if (AMODE == 1 && args.N > 2 * args.proj_width && !make_tmap_f16(&mA2, op.a_c, args.M, args.K, BM))
+    return cudaErrorInvalidValue;
   if (C::NB == 2 && !make_tmap_f16(&mB1, op.b_lo, args.N, args.K, BN)) return cudaErrorInvalidValue;
   const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
   int grid = std::min(tiles, g_num_sms(dev));
   if (max_ctas > 0) grid = std::min(grid, max_ctas);
   if (grid <= 0) return cudaSuccess;
-  kern<<<grid, kGemmThreads, C::SMEM, st>>>(mA0, mA1, mB0, mB1, args);
+  kern<<<grid, kGemmThreads, C::SMEM, st>>>(mA0, mA1, mB0, mB1, mA2, args);
   return cudaGetLastError();
 }
 
 cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args, cudaStream_t st,
-                        int max_ctas) {
+                        int max_ctas, int amode) {
   if (args.K % BK != 0 || args.N % bn != 0 || args.M <= 0) return cudaErrorInvalidValue;
-#define G4M_CASE(BN_, T_, E_) \
-  if (bn == BN_ && terms == T_ && epi == E_) return launch_t<BN_, T_, E_>(op, args, st, max_ctas);
-  G4M_CASE(256, 1, EPI_F32)
-  G4M_CASE(256, 2, EPI_F32)
-  G4M_CASE(128, 3, EPI_F32)
-  G4M_CASE(256, 2, EPI_GELU_GATE)
-  G4M_CASE(256, 2, EPI_GLU)
-  G4M_CASE(256, 2, EPI_SILU)
-  G4M_CASE(256, 2, EPI_QKV_VISION)
-  G4M_CASE(256, 2, EPI_PATCH)
+#define G4M_CASE(BN_, T_, E_, A_) \
+  if (bn == BN_ && terms == T_ && epi == E_ && amode == A_) return launch_t<BN_, T_, E_, A_>(op, args, st, max_ctas);
+  G4M_CASE(256, 1, EPI_F32, 0)
+  G4M_CASE(256, 2, EPI_F32, 0)
+  G4M_CASE(128, 3, EPI_F32, 0)
+  G4M_CASE(256, 2, EPI_GELU_GATE, 0)
+  G4M_CASE(256, 2, EPI_GLU, 0)
+  G4M_CASE(256, 2, EPI_SILU, 0)
+  G4M_CASE(256, 2, EPI_QKV_VISION, 0)
+  G4M_CASE(256, 2, EPI_PATCH, 0)
+  // integer-code operands (static input quantisation)
+  G4M_CASE(256, 1, EPI_F32, 1)
+  G4M_CASE(256, 1, EPI_QKV_VISION, 1)
+  G4M_CASE(256, 1, EPI_GELU_GATE, 2)
+  G4M_CASE(256, 1, EPI_SILU, 0)
+  G4M_CASE(256, 1, EPI_GLU, 0)
 #undef G4M_CASE
   return cudaErrorInvalidValue;
 }
@@ -544,9 +588,7 @@ __global__ void prep_a_kernel(const float* __restrict__ x, long rows, int cols, 
     if (row_scale) v = v * row_scale[i / cols];
     __half h, l;
     if (s_in != 0.0f) {
-      float r = js_round_f(__fdiv_rn(v, s_in));
-      r = fminf(fmaxf(r, -128.0f), 127.0f);
-      h = __float2half_rn(r);
+      h = __float2half_rn(srq_code(v, s_in));
       l = __float2half_rn(0.0f);
     } else {
       split_f16(v, h, l);

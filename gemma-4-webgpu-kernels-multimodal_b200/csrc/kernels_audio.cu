@@ -255,7 +255,7 @@ __global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict
                                                          const int* __restrict__ blk_index,
                                                          const int* __restrict__ row0, const int* __restrict__ rows,
                                                          float kscale, float softcap, __half* __restrict__ o_hi,
-                                                         __half* __restrict__ o_lo) {
+                                                         __half* __restrict__ o_lo, float s_code) {
   constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, D = 1024;
   __shared__ float ks[CTX][HD], vs[CTX][HD], rk[PL][HD];
   const int head = blockIdx.y;
@@ -319,21 +319,25 @@ __global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict
     const long orow = r0 + lr;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      __half h, l;
-      split_f16(o[j], h, l);
-      o_hi[orow * D + head * HD + lane + 32 * j] = h;
-      o_lo[orow * D + head * HD + lane + 32 * j] = l;
+      if (s_code != 0.0f) {  // integer codes for the post projection's input scale
+        o_hi[orow * D + head * HD + lane + 32 * j] = __float2half_rn(srq_code(o[j], s_code));
+      } else {
+        __half h, l;
+        split_f16(o[j], h, l);
+        o_hi[orow * D + head * HD + lane + 32 * j] = h;
+        o_lo[orow * D + head * HD + lane + 32 * j] = l;
+      }
     }
   }
 }
 
 cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
                                    const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
-                                   float softcap, __half* o_hi, __half* o_lo, cudaStream_t st) {
+                                   float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st) {
   if (nblocks <= 0) return cudaSuccess;
   dim3 grid(nblocks, 8);
   audio_attn_kernel<<<grid, 128, 0, st>>>(qkv, relk, qmul, blk_clip, blk_index, row0, rows, kscale, softcap, o_hi,
-                                          o_lo);
+                                          o_lo, s_code);
   return cudaGetLastError();
 }
 
@@ -341,12 +345,14 @@ cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const fl
 // Light-conv middle: causal depthwise conv (kernel 5, left pad 4) within the
 // clip (runAudioDepthwiseCausalConv1dCpu, src/audio/kernels.ts:855-884),
 // conv_norm RMSNorm, SiLU (runSiluActivationCpu) -> fp16 hi/lo operand of
-// linear_end.  One warp per row, d = 1024.  dw: [1024][5].
+// linear_end (integer codes when s_code, linear_end's input scale, is non-zero).
+// One warp per row, d = 1024.  dw: [1024][5].
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) lconv_kernel(const float* __restrict__ g, const float* __restrict__ dw,
                                                     const float* __restrict__ nw, const int* __restrict__ row_clip,
                                                     const int* __restrict__ row0, long nrows, float eps,
-                                                    __half* __restrict__ a_hi, __half* __restrict__ a_lo) {
+                                                    __half* __restrict__ a_hi, __half* __restrict__ a_lo,
+                                                    float s_code) {
   constexpr int D = 1024, V = D / 128, KS = 5;
   const int lane = threadIdx.x & 31;
   const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -383,18 +389,19 @@ __global__ void __launch_bounds__(256) lconv_kernel(const float* __restrict__ g,
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const float s = v[u] / (1.0f + expf(-v[u]));
-      split_f16(s, hh[u], ll[u]);
+      if (s_code != 0.0f) hh[u] = __float2half_rn(srq_code(s, s_code));
+      else split_f16(s, hh[u], ll[u]);
     }
     const int c = 4 * (lane + 32 * i);
     *reinterpret_cast<uint2*>(a_hi + row * D + c) = *reinterpret_cast<uint2*>(hh);
-    *reinterpret_cast<uint2*>(a_lo + row * D + c) = *reinterpret_cast<uint2*>(ll);
+    if (s_code == 0.0f) *reinterpret_cast<uint2*>(a_lo + row * D + c) = *reinterpret_cast<uint2*>(ll);
   }
 }
 
 cudaError_t audio_lconv_rows(const float* g, const float* dw, const float* nw, const int* row_clip, const int* row0,
-                             long rows, float eps, __half* a_hi, __half* a_lo, cudaStream_t st) {
+                             long rows, float eps, __half* a_hi, __half* a_lo, float s_code, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  lconv_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(g, dw, nw, row_clip, row0, rows, eps, a_hi, a_lo);
+  lconv_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(g, dw, nw, row_clip, row0, rows, eps, a_hi, a_lo, s_code);
   return cudaGetLastError();
 }
 

@@ -18,11 +18,6 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__device__ __forceinline__ float js_round_r(float x) {
-  float f = floorf(x);
-  return (x - f >= 0.5f) ? f + 1.0f : f;
-}
-
 template <int V>
 __device__ __forceinline__ float inv_rms(const float4 (&x)[V], int d, float eps) {
   float ss = 0.f;
@@ -85,23 +80,26 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(RowArgs r) {
     const float4* w = reinterpret_cast<const float4*>(r.w_next);
     __half* ah = r.a_hi + row * r.lda;
     __half* al = r.a_lo + row * r.lda;
+    __half* ac = r.a_c ? r.a_c + row * r.lda : nullptr;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       const float4 wv = w[lane + 32 * i];
       float v[4] = {(h[i].x * inv) * wv.x, (h[i].y * inv) * wv.y, (h[i].z * inv) * wv.z, (h[i].w * inv) * wv.w};
-      __align__(8) __half hh[4], ll[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (r.s_in_next != 0.0f) {
-          float q = js_round_r(__fdiv_rn(v[u], r.s_in_next));
-          q = fminf(fmaxf(q, -128.0f), 127.0f);
-          hh[u] = __float2half_rn(q);
-          ll[u] = __float2half_rn(0.0f);
-        } else {
-          split_f16(v[u], hh[u], ll[u]);
-        }
-      }
+      __align__(8) __half hh[4], ll[4], cc[4];
       const int c = 4 * (lane + 32 * i);
+      if (r.s_in_next != 0.0f) {
+        // integer codes per consumer scale: a_hi (s_in_next), a_lo (s_in_b), a_c (s_in_c)
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          hh[u] = __float2half_rn(srq_code(v[u], r.s_in_next));
+          ll[u] = __float2half_rn(r.s_in_b != 0.0f ? srq_code(v[u], r.s_in_b) : 0.0f);
+          if (ac) cc[u] = __float2half_rn(srq_code(v[u], r.s_in_c));
+        }
+        if (ac) *reinterpret_cast<uint2*>(ac + c) = *reinterpret_cast<uint2*>(cc);
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) split_f16(v[u], hh[u], ll[u]);
+      }
       *reinterpret_cast<uint2*>(ah + c) = *reinterpret_cast<uint2*>(hh);
       *reinterpret_cast<uint2*>(al + c) = *reinterpret_cast<uint2*>(ll);
     }

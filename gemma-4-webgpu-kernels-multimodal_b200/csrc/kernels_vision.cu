@@ -110,7 +110,7 @@ cudaError_t vision_pool_operand(const float* h, const int* pool_idx, int n_image
 __global__ void __launch_bounds__(128) attn_simt_kernel(const __half* __restrict__ qh, const __half* __restrict__ ql,
                                                         const __half* __restrict__ kh, const __half* __restrict__ kl,
                                                         const __half* __restrict__ vth,
-                                                        const __half* __restrict__ vtl, int n, int vt_pitch,
+                                                        const __half* __restrict__ vtl, int n, int vt_pitch, float s_code,
                                                         int heads, __half* __restrict__ oh,
                                                         __half* __restrict__ ol) {
   __shared__ float Ks[64][65];
@@ -175,19 +175,23 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const __half* __restrict
   __half* dl = ol + orow * (size_t)(heads * 64) + head * 64;
 #pragma unroll
   for (int d = 0; d < 64; ++d) {
-    __half h, lo;
-    split_f16(o[d] * inv, h, lo);
-    dh[d] = h;
-    dl[d] = lo;
+    if (s_code != 0.0f) {  // integer codes for the o_proj input scale
+      dh[d] = __float2half_rn(srq_code(o[d] * inv, s_code));
+    } else {
+      __half h, lo;
+      split_f16(o[d] * inv, h, lo);
+      dh[d] = h;
+      dl[d] = lo;
+    }
   }
 }
 
 cudaError_t vision_attention_simt(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
                                   const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
-                                  __half* o_hi, __half* o_lo, cudaStream_t st) {
+                                  __half* o_hi, __half* o_lo, float s_code, cudaStream_t st) {
   if (bh <= 0 || n <= 0) return cudaSuccess;
   dim3 grid((n + 127) / 128, bh);
-  attn_simt_kernel<<<grid, 128, 0, st>>>(q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo, n, vt_pitch, heads, o_hi, o_lo);
+  attn_simt_kernel<<<grid, 128, 0, st>>>(q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo, n, vt_pitch, s_code, heads, o_hi, o_lo);
   return cudaGetLastError();
 }
 

@@ -366,6 +366,10 @@ static int ensure_vision_buffers(Device& d, int B, int N, long E) {
       ensure(b.vt_hi, VT * f16) || ensure(b.vt_lo, VT * f16) || ensure(b.e_hi, E * 768 * f16) ||
       ensure(b.e_lo, E * 768 * f16))
     return fail(G4M_E_CUDA, "vision activation allocation failed (" + std::to_string(M) + " rows)");
+  bool codes3 = false;  // a third code plane for layers with quantised q / k / v
+  for (int i = 0; i < d.vw.layers; ++i) codes3 = codes3 || d.vw.L[i].sin_qkv[0] != 0.0f;
+  if (codes3 && ensure(b.a_c, M * 768 * f16))
+    return fail(G4M_E_CUDA, "vision activation allocation failed (" + std::to_string(M) + " rows)");
   return G4M_OK;
 }
 
@@ -382,9 +386,20 @@ static GemmArgs base_args(Device& d, int M, int N, int K) {
   a.N = N;
   a.K = K;
   a.row_scale = 1.0f;
+  a.row_scale_b = 1.0f;
+  a.row_scale_c = 1.0f;
   a.eps = 1e-6f;
   a.err = d.err;
   return a;
+}
+
+// Next-operand fields of a row pass whose consumers have input scales s[0..n)
+// (integer code planes a_hi, a_lo, a_c when they are non-zero).
+static void next_scales(RowArgs& r, const float* s, int n, __half* a_c) {
+  r.s_in_next = s ? s[0] : 0.0f;
+  r.s_in_b = (s && n > 1) ? s[1] : 0.0f;
+  r.s_in_c = (s && n > 2) ? s[2] : 0.0f;
+  r.a_c = (s && n > 2 && s[0] != 0.0f) ? a_c : nullptr;
 }
 
 // Runs vision layers [first, first+count): on entry vb.h holds the residual
@@ -396,9 +411,16 @@ static int vision_layer_range(g4m_ctx* ctx, Device& d, int B, int N, int first, 
   for (int i = first; i < first + count; ++i) {
     if (ctx->cancel.load()) return fail(G4M_E_CANCELLED, "Aborted");
     const VisionLayer& L = vw.L[i];
+    const bool qkv_codes = L.sin_qkv[0] != 0.0f;  // groups are all-zero or all-non-zero (vision_check_quant)
+    const bool gu_codes = L.sin_gu[0] != 0.0f;
     // q, k, v projections + head norms + RoPE (src/vision/encoder.ts:681-724)
     GemmArgs a = base_args(d, M, 3 * D, D);
     a.col_scale = L.sqkv;
+    if (qkv_codes) {
+      a.row_scale = L.sin_qkv[0];
+      a.row_scale_b = L.sin_qkv[1];
+      a.row_scale_c = L.sin_qkv[2];
+    }
     a.s_out = L.sout_qkv[0];
     a.s_out_b = L.sout_qkv[1];
     a.s_out_c = L.sout_qkv[2];
@@ -415,17 +437,18 @@ static int vision_layer_range(g4m_ctx* ctx, Device& d, int B, int N, int first, 
     a.k_lo = (__half*)b.k_lo.p;
     a.vt_hi = (__half*)b.vt_hi.p;
     a.vt_lo = (__half*)b.vt_lo.p;
-    GemmOperands op{(const __half*)b.a_hi.p, (const __half*)b.a_lo.p, L.wqkv, nullptr};
-    G4M_RUN("gemm_qkv", gemm_launch(256, 2, EPI_QKV_VISION, op, a, st));
+    GemmOperands op{(const __half*)b.a_hi.p, (const __half*)b.a_lo.p, L.wqkv, nullptr, (const __half*)b.a_c.p};
+    if (qkv_codes) G4M_RUN("gemm_qkv", gemm_launch(256, 1, EPI_QKV_VISION, op, a, st, 0, 1));
+    else G4M_RUN("gemm_qkv", gemm_launch(256, 2, EPI_QKV_VISION, op, a, st));
     // attention body (src/vision/kernels.ts:75-114), scale 1
     if (ctx->attention_impl == 0) {
       G4M_RUN("attention", vision_attention_tc((const __half*)b.q_hi.p, (const __half*)b.q_lo.p, (const __half*)b.k_hi.p,
                                      (const __half*)b.k_lo.p, (const __half*)b.vt_hi.p, (const __half*)b.vt_lo.p, B * 12,
-                                     N, vt_pitch(N), 12, (__half*)b.o_hi.p, (__half*)b.o_lo.p, d.err, st));
+                                     N, vt_pitch(N), 12, (__half*)b.o_hi.p, (__half*)b.o_lo.p, L.sin_o, d.err, st));
     } else {
       G4M_RUN("attention", vision_attention_simt((const __half*)b.q_hi.p, (const __half*)b.q_lo.p, (const __half*)b.k_hi.p,
                                        (const __half*)b.k_lo.p, (const __half*)b.vt_hi.p, (const __half*)b.vt_lo.p,
-                                       B * 12, N, vt_pitch(N), 12, (__half*)b.o_hi.p, (__half*)b.o_lo.p, st));
+                                       B * 12, N, vt_pitch(N), 12, (__half*)b.o_hi.p, (__half*)b.o_lo.p, L.sin_o, st));
     }
     // o_proj
     a = base_args(d, M, D, D);
@@ -433,8 +456,9 @@ static int vision_layer_range(g4m_ctx* ctx, Device& d, int B, int N, int first, 
     a.s_out = L.sout_o;
     a.out_f32 = (float*)b.y.p;
     a.ldo = D;
-    op = GemmOperands{(const __half*)b.o_hi.p, (const __half*)b.o_lo.p, L.wo, nullptr};
-    G4M_RUN("gemm_o", gemm_launch(256, 2, EPI_F32, op, a, st));
+    if (L.sin_o != 0.0f) a.row_scale = L.sin_o;
+    op = GemmOperands{(const __half*)b.o_hi.p, (const __half*)b.o_lo.p, L.wo, nullptr, nullptr};
+    G4M_RUN("gemm_o", gemm_launch(256, L.sin_o != 0.0f ? 1 : 2, EPI_F32, op, a, st));
     // post-attention norm + residual + pre-feedforward norm
     RowArgs r;
     memset(&r, 0, sizeof(r));
@@ -447,6 +471,7 @@ static int vision_layer_range(g4m_ctx* ctx, Device& d, int B, int N, int first, 
     r.h_in = (const float*)b.h.p;
     r.h_out = (float*)b.h.p;
     r.w_next = L.n_pf;
+    next_scales(r, L.sin_gu, 2, nullptr);
     r.a_hi = (__half*)b.a_hi.p;
     r.a_lo = (__half*)b.a_lo.p;
     r.lda = D;
@@ -459,33 +484,42 @@ static int vision_layer_range(g4m_ctx* ctx, Device& d, int B, int N, int first, 
     a.out_hi = (__half*)b.g_hi.p;
     a.out_lo = (__half*)b.g_lo.p;
     a.ldh = 3072;
-    op = GemmOperands{(const __half*)b.a_hi.p, (const __half*)b.a_lo.p, L.wgu, nullptr};
-    G4M_RUN("gemm_gate_up", gemm_launch(256, 2, EPI_GELU_GATE, op, a, st));
+    a.s_code = L.sin_d;  // down_proj's input scale: store codes
+    if (gu_codes) {
+      a.row_scale = L.sin_gu[0];
+      a.row_scale_b = L.sin_gu[1];
+    }
+    op = GemmOperands{(const __half*)b.a_hi.p, (const __half*)b.a_lo.p, L.wgu, nullptr, nullptr};
+    if (gu_codes) G4M_RUN("gemm_gate_up", gemm_launch(256, 1, EPI_GELU_GATE, op, a, st, 0, 2));
+    else G4M_RUN("gemm_gate_up", gemm_launch(256, 2, EPI_GELU_GATE, op, a, st));
     // down_proj
     a = base_args(d, M, D, 3072);
     a.col_scale = L.sd;
     a.s_out = L.sout_d;
     a.out_f32 = (float*)b.y.p;
     a.ldo = D;
-    op = GemmOperands{(const __half*)b.g_hi.p, (const __half*)b.g_lo.p, L.wd, nullptr};
-    G4M_RUN("gemm_down", gemm_launch(256, 2, EPI_F32, op, a, st));
+    if (L.sin_d != 0.0f) a.row_scale = L.sin_d;
+    op = GemmOperands{(const __half*)b.g_hi.p, (const __half*)b.g_lo.p, L.wd, nullptr, nullptr};
+    G4M_RUN("gemm_down", gemm_launch(256, L.sin_d != 0.0f ? 1 : 2, EPI_F32, op, a, st));
     // post-feedforward norm + residual (+ next layer's input norm)
     r.w_post = L.n_po;
-    r.w_next = (i + 1 < first + count) ? vw.L[i + 1].n_in : nullptr;
+    const bool more = i + 1 < first + count;
+    r.w_next = more ? vw.L[i + 1].n_in : nullptr;
+    next_scales(r, more ? vw.L[i + 1].sin_qkv : nullptr, 3, (__half*)b.a_c.p);
     G4M_RUN("rows", fused_rows(r, st));
   }
   return G4M_OK;
 }
 
+// Projections that share an operand must all use static input quantisation
+// or none of them (q / k / v, gate / up); the rest is per linear.
 static int vision_check_quant(const VisionWeights& vw, int layers) {
   for (int i = 0; i < layers; ++i) {
     const VisionLayer& L = vw.L[i];
-    if (L.sin_qkv[0] != 0 || L.sin_qkv[1] != 0 || L.sin_qkv[2] != 0 || L.sin_o != 0 || L.sin_gu[0] != 0 ||
-        L.sin_gu[1] != 0 || L.sin_d != 0)
-      return fail(G4M_E_UNSUPPORTED,
-                  "vision layer " + std::to_string(i) +
-                      ": static input-activation quantisation (input_activation_scale != 0) is not supported by the "
-                      "fused tower path; use g4m_qat_linear for quantised single linears");
+    if (quant_group(L.sin_qkv, 3) < 0 || quant_group(L.sin_gu, 2) < 0)
+      return fail(G4M_E_UNSUPPORTED, "vision layer " + std::to_string(i) +
+                                         ": q/k/v (or gate/up) projections mix zero and non-zero "
+                                         "input_activation_scale; they share one operand");
   }
   return G4M_OK;
 }
@@ -541,6 +575,7 @@ int vision_forward(g4m_ctx* ctx, Device& d, int B, const float* pix_dev, int H, 
   r.eps = 1e-6f;
   r.h_in = (const float*)b.h.p;
   r.w_next = vw.L[0].n_in;
+  next_scales(r, vw.L[0].sin_qkv, 3, (__half*)b.a_c.p);
   r.a_hi = (__half*)b.a_hi.p;
   r.a_lo = (__half*)b.a_lo.p;
   r.lda = D;
@@ -891,6 +926,7 @@ int g4m_vision_layers(g4m_ctx* ctx, int di, int n, int height, int width, int fi
   r.eps = 1e-6f;
   r.h_in = (const float*)b.h.p;
   r.w_next = d.vw.L[first].n_in;
+  next_scales(r, d.vw.L[first].sin_qkv, 3, (__half*)b.a_c.p);
   r.a_hi = (__half*)b.a_hi.p;
   r.a_lo = (__half*)b.a_lo.p;
   r.lda = 768;

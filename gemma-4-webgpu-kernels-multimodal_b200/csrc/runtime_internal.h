@@ -98,13 +98,22 @@ struct LayoutCache {
 };
 
 struct VisionBuffers {
-  DevBuf h, y, h0, a_hi, a_lo, o_hi, o_lo, g_hi, g_lo, q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo, e_hi, e_lo;
+  DevBuf h, y, h0, a_hi, a_lo, a_c, o_hi, o_lo, g_hi, g_lo, q_hi, q_lo, k_hi, k_lo, vt_hi, vt_lo, e_hi, e_lo;
 };
 
 struct AudioBuffers {
   DevBuf samples, sample_off, sample_len, frame_off, frames, feats, fmask, t0_off, t0_len, l0, l0mask, t1_off, t1_len,
-      l1, row_clip, clip_row0, clip_rows, h, y, qkv, g, a_hi, a_lo, f_hi, f_lo, keep, proj, e_hi, e_lo, out, h0;
+      l1, row_clip, clip_row0, clip_rows, h, y, qkv, g, a_hi, a_lo, a_c, f_hi, f_lo, keep, proj, e_hi, e_lo, out, h0;
 };
+
+// Static input quantisation of projections sharing one operand (q / k / v,
+// gate / up): 0 all scales zero (hi/lo operand), 1 all non-zero (one code
+// plane per scale), -1 mixed (not supported).
+inline int quant_group(const float* s, int n) {
+  int nz = 0;
+  for (int i = 0; i < n; ++i) nz += s[i] != 0.0f;
+  return nz == 0 ? 0 : (nz == n ? 1 : -1);
+}
 
 // Opt-in per-launch event timing (g4m_profile_begin / g4m_profile_end).
 struct ProfRec {
@@ -148,14 +157,14 @@ struct Device {
     ev_pool.clear();
     for (void* p : allocs) cudaFree(p);
     allocs.clear();
-    DevBuf* bufs[] = {&vb.h, &vb.y, &vb.h0, &vb.a_hi, &vb.a_lo, &vb.o_hi, &vb.o_lo, &vb.g_hi, &vb.g_lo,
+    DevBuf* bufs[] = {&vb.h, &vb.y, &vb.h0, &vb.a_hi, &vb.a_lo, &vb.a_c, &vb.o_hi, &vb.o_lo, &vb.g_hi, &vb.g_lo,
                       &vb.q_hi, &vb.q_lo, &vb.k_hi, &vb.k_lo, &vb.vt_hi, &vb.vt_lo, &vb.e_hi, &vb.e_lo,
                       &vlc.pos_xy, &vlc.rope, &vlc.pool, &io_in, &io_out};
     for (DevBuf* b : bufs) release(*b);
     DevBuf* abufs[] = {&ab.samples, &ab.sample_off, &ab.sample_len, &ab.frame_off, &ab.frames, &ab.feats,
                        &ab.fmask, &ab.t0_off, &ab.t0_len, &ab.l0, &ab.l0mask, &ab.t1_off, &ab.t1_len, &ab.l1,
                        &ab.row_clip, &ab.clip_row0, &ab.clip_rows, &ab.h, &ab.y, &ab.qkv, &ab.g, &ab.a_hi,
-                       &ab.a_lo, &ab.f_hi, &ab.f_lo, &ab.keep, &ab.proj, &ab.e_hi, &ab.e_lo, &ab.out, &ab.h0};
+                       &ab.a_lo, &ab.a_c, &ab.f_hi, &ab.f_lo, &ab.keep, &ab.proj, &ab.e_hi, &ab.e_lo, &ab.out, &ab.h0};
     for (DevBuf* b : abufs) release(*b);
     if (err) cudaFree(err);
     err = nullptr;

@@ -151,10 +151,11 @@ G4M_API int g4m_audio_embed_device(g4m_ctx* ctx, int device_index, int n, const 
                            const int64_t* lengths, int sampling_rate, int layer_count, int64_t max_samples,
                            float* out_dev, int* rows_out, void* stream);
 
-/* Stage outputs of the last audio call on a device, packed rows [rows][1024],
- * for stage-anchored parity checks: which = 0 encoder input (after the
- * subsample input projection; needs g4m_set_debug), 1 encoder output (after
- * norm_out of the last layer). */
+/* Stage outputs of the last audio call on a device, packed rows, for
+ * stage-anchored parity checks: which = 0 encoder input [rows][1024] (after
+ * the subsample input projection; needs g4m_set_debug), 1 encoder output
+ * [rows][1024] (after norm_out of the last layer), 2 the q | k | v
+ * projections of the last layer run [rows][3072]. */
 G4M_API int g4m_audio_debug_hidden(g4m_ctx* ctx, int device_index, int which, float* host, size_t count);
 
 /* Run conformer layers [first, first+count) on host hidden states h

@@ -408,7 +408,42 @@ def _vis(W, i, name):
     return f"model.vision_tower.encoder.layers.{i}.{name}"
 
 
+# Optional recorder of each QAT linear's input absmax (record_linear_inputs),
+# for calibrating static input-activation scales on a real pass.
+_TAPS: Optional[Dict[str, float]] = None
+
+
+class record_linear_inputs:
+    """Context manager: while active, every QAT linear run by the layer
+    compositions below records max |x| of its input under its tensor prefix."""
+
+    def __enter__(self):
+        global _TAPS
+        _TAPS = {}
+        return _TAPS
+
+    def __exit__(self, *exc):
+        global _TAPS
+        _TAPS = None
+        return False
+
+
+def _tap(prefix, x):
+    if _TAPS is not None:
+        _TAPS[prefix] = max(_TAPS.get(prefix, 0.0), float(np.abs(np.asarray(x, np.float64)).max()))
+
+
+def calibrated_input_scales(W: Dict[str, np.ndarray], absmax: Dict[str, float]) -> Dict[str, np.ndarray]:
+    """Copy of W whose input_activation_scale is absmax/127 (fround) for every
+    recorded linear: the calibrated static-quantisation mode."""
+    out = dict(W)
+    for prefix, m in absmax.items():
+        out[f"{prefix}.input_activation_scale"] = np.array(np.float32(m / 127.0) if m > 0 else 1.0, np.float32).reshape(())
+    return out
+
+
 def _qat_vision(W, prefix, x):
+    _tap(prefix, x)
     return qat_i8_linear(x, W[f"{prefix}.weight"], W[f"{prefix}.weight_scale"], float(W[f"{prefix}.input_activation_scale"]),
                          float(W[f"{prefix}.output_activation_scale"]))
 
@@ -467,6 +502,7 @@ def _aud(i, name):
 
 
 def _packed(W, prefix, x, inp, out):
+    _tap(prefix, x)
     w = W[f"{prefix}.weight"]
     bits = derive_packed_bits(w.nbytes, inp, out)
     return packed_qat_linear(x, w, W[f"{prefix}.weight_scale"], inp, out, bits, float(W[f"{prefix}.input_activation_scale"]),
@@ -488,13 +524,17 @@ def audio_relative_keys(W, i) -> np.ndarray:
     return f32_linear_rows(audio_relpos(c["plen"], c["hidden"]), W[_aud(i, "self_attn.relative_k_proj.weight")])
 
 
+def audio_qkv(W, i, x):
+    """q, k, v projections of audio layer i (src/audio/encoder.ts:1019-1036)."""
+    d = AUDIO["hidden"]
+    return tuple(_packed(W, _aud(i, f"self_attn.{p}_proj.linear"), x, d, d) for p in "qkv")
+
+
 def audio_attention_block(W, i, x):
     """computeAudioSelfAttentionGpuOnly dataflow, src/audio/encoder.ts:1011-1071."""
     c = AUDIO
     d = c["hidden"]
-    q = _packed(W, _aud(i, "self_attn.q_proj.linear"), x, d, d)
-    k = _packed(W, _aud(i, "self_attn.k_proj.linear"), x, d, d)
-    v = _packed(W, _aud(i, "self_attn.v_proj.linear"), x, d, d)
+    q, k, v = audio_qkv(W, i, x)
     rk = audio_relative_keys(W, i)
     o = audio_attention(q, k, v, rk, W[_aud(i, "self_attn.per_dim_scale")], c["heads"], c["head_dim"], c["chunk"], c["ctx"],
                         c["plen"], c["softcap"])
