@@ -41,14 +41,25 @@ def env_int(k, d):
         return d
 
 
-def weights_path(layers: int, rank: int, barrier) -> str:
+def s_in_mode(quant: str):
+    """input_activation_scale of every QAT linear: 0 (no static input
+    quantisation) or the fixed per-linear absmax/127 table ("calibrated")."""
+    return "calibrated" if quant == "calibrated" else 0.0
+
+
+QUANT_DESC = {"none": "none (input_activation_scale 0: fp16 hi/lo activations, two-term GEMMs)",
+              "calibrated": "calibrated (input_activation_scale = absmax/127 per linear: int8 codes, one-term GEMMs)"}
+
+
+def weights_path(tower: str, layers: int, quant: str, rank: int, barrier) -> str:
     syn = importlib.import_module(PKG + ".synthetic")
     d = os.path.join(os.environ.get("TMPDIR", "/tmp"), "g4m_bench")
     os.makedirs(d, exist_ok=True)
-    p = os.path.join(d, f"vision{layers}_seed0.safetensors")
+    p = os.path.join(d, f"{tower}{layers}_seed0_{quant}.safetensors")
     if rank == 0 and not os.path.exists(p):
         tmp = p + f".tmp{os.getpid()}"
-        syn.write_safetensors(tmp, syn.vision_weights(0, layers=layers))
+        make = syn.vision_weights if tower == "vision" else syn.audio_weights
+        syn.write_safetensors(tmp, make(0, layers=layers, s_in=s_in_mode(quant)))
         os.replace(tmp, p)
     barrier()
     return p
@@ -125,7 +136,7 @@ def vision_kernel_flops(B: int, N: int, tokens: int):
     }
 
 
-def cpu_vision_sample(threads: int):
+def cpu_vision_sample(threads: int, quant: str = "none"):
     """Oracle (CPU restatement of the reference's CPU twins) on one 768x768
     image: patch embedding + one encoder layer + pooler/embedder, scaled to
     16 layers.  Returns (seconds per image, description)."""
@@ -133,7 +144,7 @@ def cpu_vision_sample(threads: int):
     import oracle as O
     syn = importlib.import_module(PKG + ".synthetic")
     O.set_threads(threads)
-    W = syn.vision_weights(0, layers=1)
+    W = syn.vision_weights(0, layers=1, s_in=s_in_mode(quant))
     pix = syn.image_pixels(0, 768, 768)
     pre = O.preprocess_image_pixels(pix)
     patches, pos = O.valid_image_patch_input(pre)
@@ -173,7 +184,7 @@ def audio_rows(n: int) -> int:
     return (t0 - 1) // 2 + 1 if f else 0
 
 
-def cpu_audio_sample(threads: int):
+def cpu_audio_sample(threads: int, quant: str = "none"):
     """Oracle on one 10 s clip (cfg2): log-mel + subsample + one of 12
     conformer layers (x12) + output projection / embedder.  Returns (seconds
     of compute per second of audio, description)."""
@@ -181,7 +192,7 @@ def cpu_audio_sample(threads: int):
     import oracle as O
     syn = importlib.import_module(PKG + ".synthetic")
     O.set_threads(threads)
-    W = syn.audio_weights(0, layers=1)
+    W = syn.audio_weights(0, layers=1, s_in=s_in_mode(quant))
     x = syn.audio_samples(0, 160000)
     t0 = time.perf_counter()
     pre = O.preprocess_audio(x, pad_to_multiple_of=None)
@@ -204,7 +215,7 @@ def run_reference(args):
     secs = []
     desc = ""
     for i in range(args.warmup + args.steps):
-        s, desc = cpu_vision_sample(threads)
+        s, desc = cpu_vision_sample(threads, args.quant)
         if i >= args.warmup:
             secs.append(s)
     value = len(secs) / sum(secs)
@@ -214,13 +225,13 @@ def run_reference(args):
         "ms_per_step": 1000.0 * sum(secs) / len(secs), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (JS number / Math.fround semantics)", "data": "synthetic",
         "config": {"workload": "vision batch, 768x768 images, 16 layers, reference CPU path (bounded sample)",
-                   "image": "768x768", "layers": 16},
+                   "image": "768x768", "layers": 16, "activation_quant": QUANT_DESC[args.quant]},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
     if not args.no_audio:
-        a_secs = [cpu_audio_sample(threads)[0] for _ in range(max(1, min(args.steps, 3)))]
+        a_secs = [cpu_audio_sample(threads, args.quant)[0] for _ in range(max(1, min(args.steps, 3)))]
         av = len(a_secs) / sum(a_secs)
         line["audio"] = {"metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": av,
                          "unit": "audio-s/s", "cpu_baseline": {"value": av, "unit": "audio-s/s", "cores": threads,
@@ -233,13 +244,7 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     without padding rows.  Returns the sub-object of the JSON line (rank 0)."""
     import numpy as np
     import torch
-    d = os.path.join(os.environ.get("TMPDIR", "/tmp"), "g4m_bench")
-    p = os.path.join(d, "audio12_seed0.safetensors")
-    if rank == 0 and not os.path.exists(p):
-        tmp = p + f".tmp{os.getpid()}"
-        syn.write_safetensors(tmp, syn.audio_weights(0, layers=12))
-        os.replace(tmp, p)
-    barrier()
+    p = weights_path("audio", 12, args.quant, rank, barrier)
     ctx = ctx_cls([torch.cuda.current_device()])
     ctx.load_weights(p)
     n = args.clips
@@ -262,11 +267,13 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     torch.cuda.synchronize()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches0 = native.kernel_launches()
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
     e1.synchronize()
+    launches = native.kernel_launches() - launches0
     t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -296,7 +303,9 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
         "metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": value, "unit": "audio-s/s",
         "ms_per_step": ms / args.steps,
         "config": {"workload": f"batched audio: {n} clips/GPU, lengths U[1,30] s (seeded), packed rows (no padding)",
-                   "clips_per_gpu": n, "audio_seconds_per_gpu": audio_seconds, "encoder_rows_per_gpu": rows},
+                   "clips_per_gpu": n, "audio_seconds_per_gpu": audio_seconds, "encoder_rows_per_gpu": rows,
+                   "activation_quant": QUANT_DESC[args.quant]},
+        "gpu_launches": launches,
         "e2e": {"value": world * audio_seconds * k_e2e / float(te.item()), "unit": "audio-s/s",
                 "h2d_bytes_per_step": total * 4, "d2h_bytes_per_step": rows * 1536 * 4},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
@@ -305,7 +314,7 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
         "kernel_ms_per_step": {k: round(v[1], 4) for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        spa, desc = cpu_audio_sample(os.cpu_count() or 1)
+        spa, desc = cpu_audio_sample(os.cpu_count() or 1, args.quant)
         res["cpu_baseline"] = {"value": 1.0 / spa, "unit": "audio-s/s", "cores": os.cpu_count() or 1, "kind": "port",
                                "sample": desc}
     ctx.close()
@@ -333,7 +342,7 @@ def run_ours(args):
     syn = importlib.import_module(PKG + ".synthetic")
     B, H, Wd, layers, max_soft = args.batch, 768, 768, 16, 280
     N, tokens = (H // 16) * (Wd // 16), 256
-    path = weights_path(layers, rank, barrier)
+    path = weights_path("vision", layers, args.quant, rank, barrier)
     ctx = native.Context([local])
     ctx.load_weights(path)
 
@@ -395,6 +404,15 @@ def run_ours(args):
                 "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
                 "launch_ms": tot / cnt, "flop_per_launch": flops[dom]}
     kernel_ms = {k: round(v[1], 4) for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])}
+    # the int8 QAT linears together (the metric's "int8-linear tensor-pipe % of peak")
+    qat = [k for k in ("gemm_qkv", "gemm_o", "gemm_gate_up", "gemm_down") if k in prof]
+    qat_flop = sum(flops[k] * prof[k][0] for k in qat)
+    qat_ms = sum(prof[k][1] for k in qat)
+    qat_ach = qat_flop / (qat_ms / 1000.0) / 1e12
+    qat_linear = {"kernels": qat, "achieved": qat_ach, "peak": peak, "unit": "TFLOP/s", "frac": qat_ach / peak,
+                  "peak_source": peak_src, "ms_per_step": qat_ms,
+                  "note": "algorithmic 2*M*N*K per linear (one term); the split operands execute "
+                          + ("1x" if args.quant == "calibrated" else "2x") + " that on the tensor pipe"}
 
     # end to end through the C ABI with pinned host buffers
     out_host = [np.empty((tokens, TEXT), np.float32) for _ in range(B)]
@@ -417,10 +435,9 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        s, desc = cpu_vision_sample(threads)
+        s, desc = cpu_vision_sample(threads, args.quant)
         cpu = {"value": 1.0 / s, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc}
 
-    launches_total = launches
     audio = None
     if not args.no_audio:
         ctx.close()
@@ -431,15 +448,18 @@ def run_ours(args):
             "impl": "g4m", "metric": "images/s (vision tower 768x768, 16 layers, + embedder)", "value": value,
             "unit": "images/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f32-grade (fp16 hi/lo split operands on tcgen05, f32 accumulate)",
+            "dtype": ("f32-grade (fp16 hi/lo split operands on tcgen05, f32 accumulate)" if args.quant == "none" else
+                      "int8 activation codes x int8 weights on tcgen05 (exact in fp16), f32 accumulate"),
             "data": "synthetic (seeded U[0,1] pixels, random-init weights with the reference dtypes)",
             "config": {"workload": f"batched vision: {B} images/GPU of 768x768 (2304 patches, 256 tokens), 16 layers",
                        "images_per_gpu": B, "image": "768x768", "layers": layers, "parallelism": f"dp{world} (replicas)",
-                       "l2": "inputs larger than L2 (pixels %.0f MB per GPU per step)" % (B * H * Wd * 3 * 4 / 1e6)},
+                       "l2": "inputs larger than L2 (pixels %.0f MB per GPU per step)" % (B * H * Wd * 3 * 4 / 1e6),
+                       "activation_quant": QUANT_DESC[args.quant]},
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": B * H * Wd * 3 * 4,
                     "d2h_bytes_per_step": B * tokens * TEXT * 4},
             "gpu_launches": launches,
             "roofline": roofline,
+            "qat_linear": qat_linear,
             "kernel_ms_per_step": kernel_ms,
             "cpu_baseline": cpu,
             "clocks": clk,
@@ -463,6 +483,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-audio", action="store_true", help="skip the batched-audio half of the metric")
     ap.add_argument("--clips", type=int, default=128, help="audio clips per GPU per step")
+    ap.add_argument("--quant", default="none", choices=["none", "calibrated"],
+                    help="static input-activation quantisation of the QAT linears")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -348,6 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (ok) {
       tc_fence_after();
       const float inv = 1.0f / l;
+      const float inv_code = s_code != 0.0f ? 1.0f / s_code : 0.0f;
       const int qrow = q0 + t * QT + r;
       const int img = bh / heads, head = bh % heads;
       const size_t orow = (size_t)img * n + qrow;
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   __half2 h2;
                   uint32_t w;
                 } cv;
-                cv.h2 = __floats2half2_rn(srq_code(x0, s_code), srq_code(x1, s_code));
+                cv.h2 = __floats2half2_rn(srq_code(x0, s_code, inv_code), srq_code(x1, s_code, inv_code));
                 hv[u] = cv.w;
               } else {
                 split2_f16(x0, x1, hv[u], lv[u]);

@@ -555,27 +555,34 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   if (rc) return rc;
   const int n = (int)shapes.size();
   if (n == 0) return G4M_OK;
-  std::vector<int> foff(n), fcnt(n), rows(n);
+  std::vector<int> foff(n), fcnt(n), rows(n), t0off(n);
   std::vector<long> slen(n);
-  long FR = 0;
+  long FR = 0, T0S = 0;
+  int max_t0 = 0;
   for (int i = 0; i < n; ++i) {
     foff[i] = (int)FR;
     fcnt[i] = shapes[i].frames;
     rows[i] = shapes[i].t1;
     slen[i] = shapes[i].samples;
     FR += shapes[i].frames;
+    const int t0 = (shapes[i].frames - 1) / 2 + 1;  // layer-0 rows (src/audio/kernels.ts:1242-1244)
+    t0off[i] = (int)T0S;
+    T0S += t0;
+    max_t0 = std::max(max_t0, t0);
   }
   long M = 0;
   int nblocks = 0;
   if ((rc = audio_setup_rows(d, rows, &M, &nblocks, st))) return rc;
   AudioBuffers& b = d.ab;
   if (ensure(b.sample_off, n * 8) || ensure(b.sample_len, n * 8) || ensure(b.frame_off, n * 4) ||
-      ensure(b.frames, n * 4) || ensure(b.feats, FR * 128 * 4))
+      ensure(b.frames, n * 4) || ensure(b.feats, FR * 128 * 4) || ensure(b.t0_off, n * 4) ||
+      ensure(b.l0, (size_t)T0S * 64 * 128 * 4))
     return fail(G4M_E_CUDA, "audio front-end allocation failed");
   G4M_LAUNCH_A(cudaMemcpyAsync(b.sample_off.p, soff.data(), n * 8, cudaMemcpyHostToDevice, st));
   G4M_LAUNCH_A(cudaMemcpyAsync(b.sample_len.p, slen.data(), n * 8, cudaMemcpyHostToDevice, st));
   G4M_LAUNCH_A(cudaMemcpyAsync(b.frame_off.p, foff.data(), n * 4, cudaMemcpyHostToDevice, st));
   G4M_LAUNCH_A(cudaMemcpyAsync(b.frames.p, fcnt.data(), n * 4, cudaMemcpyHostToDevice, st));
+  G4M_LAUNCH_A(cudaMemcpyAsync(b.t0_off.p, t0off.data(), n * 4, cudaMemcpyHostToDevice, st));
   G4M_LAUNCH_A(cudaStreamSynchronize(st));
   const int* dfoff = (const int*)b.frame_off.p;
   const int* dfcnt = (const int*)b.frames.p;
@@ -584,9 +591,10 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   // front end (preprocessGemma4AudioSamples + runAudioSubsampleProjectionCpu)
   G4M_RUN("logmel", audio_logmel(samples_dev, (const long*)b.sample_off.p, (const long*)b.sample_len.p, dfoff, dfcnt, n,
                                  (int)FR, aw.window, aw.mel, aw.twiddle, (float*)b.feats.p, nullptr, st));
-  G4M_RUN("subsample", audio_subsample((const float*)b.feats.p, dfoff, dfcnt, (const int*)b.clip_row0.p,
-                                       (const int*)b.clip_rows.p, (const int*)b.row_clip.p, M, aw.c0w, aw.c0n, aw.c1w,
-                                       aw.c1n, 1e-6f, ah, al, st));
+  const int max_rows = *std::max_element(rows.begin(), rows.end());
+  G4M_RUN("subsample", audio_subsample((const float*)b.feats.p, dfoff, dfcnt, (const int*)b.t0_off.p,
+                                       (const int*)b.clip_row0.p, (const int*)b.clip_rows.p, n, max_t0, max_rows,
+                                       aw.c0w, aw.c0n, aw.c1w, aw.c1n, 1e-6f, (float*)b.l0.p, ah, al, st));
   GemmArgs a = aargs(d, M, D, D);
   a.out_f32 = h;
   a.ldo = D;

@@ -9,9 +9,13 @@
 namespace g4m {
 
 // srqScalar's integer code (src/kernels/qat.ts:489-492): clamp(round(v / s),
-// -128, 127) with JS Math.round (ties toward +inf).
-__device__ __forceinline__ float srq_code(float v, float s) {
-  const float q = __fdiv_rn(v, s);
+// -128, 127) with JS Math.round (ties toward +inf).  The quotient is v * (1/s)
+// corrected once by its fma residual, q + (v - q s) / s (Markstein, IBM J.
+// Res. Develop. 34(1), 1990), which recovers the rounded quotient v / s
+// without a division per element; inv_s = 1 / s is computed once by the caller.
+__device__ __forceinline__ float srq_code(float v, float s, float inv_s) {
+  const float q0 = v * inv_s;
+  const float q = fmaf(fmaf(-q0, s, v), inv_s, q0);
   const float f = floorf(q);
   const float r = (q - f >= 0.5f) ? f + 1.0f : f;
   return fminf(fmaxf(r, -128.0f), 127.0f);
@@ -128,9 +132,12 @@ cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __
 cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
                          const int* frames, int clips, int total_frames, const float* window, const float* mel,
                          const double2* twiddle, float* features, uint8_t* mask, cudaStream_t st);
-cudaError_t audio_subsample(const float* feats, const int* frame_off, const int* frames, const int* row0,
-                            const int* rows, const int* row_clip, long total_rows, const float* w0, const float* n0,
-                            const float* w1t, const float* n1, float eps, __half* a_hi, __half* a_lo, cudaStream_t st);
+// Layer-0 rows of clip i start at packed layer-0 row t0off[i] of l0 (scratch
+// [sum T0][64][128] f32); output rows at packed row row0[i], rows[i] of them.
+cudaError_t audio_subsample(const float* feats, const int* frame_off, const int* frames, const int* t0off,
+                            const int* row0, const int* rows, int clips, int max_t0, int max_rows, const float* w0,
+                            const float* n0, const float* w1t, const float* n1, float eps, float* l0, __half* a_hi,
+                            __half* a_lo, cudaStream_t st);
 cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
                                    const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
                                    float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st);

@@ -50,7 +50,7 @@ struct GemmCfg {
 // srqScalar (src/kernels/qat.ts:489-492): clamp(round(v/s), -128, 127) * s.
 __device__ __forceinline__ float srq_f(float v, float s) {
   if (s == 0.0f) return v;
-  return srq_code(v, s) * s;
+  return srq_code(v, s, 1.0f / s) * s;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -103,6 +103,7 @@ __device__ __forceinline__ void load_scales32(const float* p, float* s) {
 
 // Codes for the next GEMM's input scale (EPI_GELU_GATE / EPI_SILU outputs).
 __device__ __forceinline__ void store_codes_row(__half* dst, const float* v, float s, int n) {
+  const float inv = 1.0f / s;
   for (int j = 0; j < n; j += 8) {
     uint32_t hv[4];
 #pragma unroll
@@ -111,7 +112,7 @@ __device__ __forceinline__ void store_codes_row(__half* dst, const float* v, flo
         __half2 h;
         uint32_t w;
       } c;
-      c.h = __floats2half2_rn(srq_code(v[j + 2 * u], s), srq_code(v[j + 2 * u + 1], s));
+      c.h = __floats2half2_rn(srq_code(v[j + 2 * u], s, inv), srq_code(v[j + 2 * u + 1], s, inv));
       hv[u] = c.w;
     }
     *reinterpret_cast<uint4*>(dst + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
@@ -583,12 +584,13 @@ cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, cons
 __global__ void prep_a_kernel(const float* __restrict__ x, long rows, int cols, float s_in, const float* row_scale,
                               __half* __restrict__ hi, __half* __restrict__ lo) {
   const long n = rows * (long)cols;
+  const float inv_s = s_in != 0.0f ? 1.0f / s_in : 0.0f;
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     float v = x[i];
     if (row_scale) v = v * row_scale[i / cols];
     __half h, l;
     if (s_in != 0.0f) {
-      h = __float2half_rn(srq_code(v, s_in));
+      h = __float2half_rn(srq_code(v, s_in, inv_s));
       l = __float2half_rn(0.0f);
     } else {
       split_f16(v, h, l);

@@ -81,6 +81,9 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(RowArgs r) {
     __half* ah = r.a_hi + row * r.lda;
     __half* al = r.a_lo + row * r.lda;
     __half* ac = r.a_c ? r.a_c + row * r.lda : nullptr;
+    const float inv_a = r.s_in_next != 0.0f ? 1.0f / r.s_in_next : 0.0f;
+    const float inv_b = r.s_in_b != 0.0f ? 1.0f / r.s_in_b : 0.0f;
+    const float inv_c = r.s_in_c != 0.0f ? 1.0f / r.s_in_c : 0.0f;
 #pragma unroll
     for (int i = 0; i < V; ++i) {
       const float4 wv = w[lane + 32 * i];
@@ -91,9 +94,9 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(RowArgs r) {
         // integer codes per consumer scale: a_hi (s_in_next), a_lo (s_in_b), a_c (s_in_c)
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          hh[u] = __float2half_rn(srq_code(v[u], r.s_in_next));
-          ll[u] = __float2half_rn(r.s_in_b != 0.0f ? srq_code(v[u], r.s_in_b) : 0.0f);
-          if (ac) cc[u] = __float2half_rn(srq_code(v[u], r.s_in_c));
+          hh[u] = __float2half_rn(srq_code(v[u], r.s_in_next, inv_a));
+          ll[u] = __float2half_rn(r.s_in_b != 0.0f ? srq_code(v[u], r.s_in_b, inv_b) : 0.0f);
+          if (ac) cc[u] = __float2half_rn(srq_code(v[u], r.s_in_c, inv_c));
         }
         if (ac) *reinterpret_cast<uint2*>(ac + c) = *reinterpret_cast<uint2*>(cc);
       } else {

@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const __half* __restrict
 #pragma unroll
   for (int d = 0; d < 64; ++d) {
     if (s_code != 0.0f) {  // integer codes for the o_proj input scale
-      dh[d] = __float2half_rn(srq_code(o[d] * inv, s_code));
+      dh[d] = __float2half_rn(srq_code(o[d] * inv, s_code, 1.0f / s_code));
     } else {
       __half h, lo;
       split_f16(o[d] * inv, h, lo);

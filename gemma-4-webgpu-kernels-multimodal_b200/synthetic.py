@@ -161,9 +161,28 @@ def _f32(seed: int, name: str, shape: Tuple[int, ...], mean: float, std: float) 
     return (mean + std * normal(seed, name, n)).astype(np.float32).reshape(shape)
 
 
-def vision_weights(seed: int = 0, layers: int = VISION_LAYERS, s_in: float = 0.0, s_out: float = 0.0) -> Dict[str, np.ndarray]:
+# Static input-activation quantisation at fixed per-linear scales: absmax/127
+# of each linear's input, with the absmax measured once on a seeded 768 x 768
+# image (vision) and a 30 s clip (audio) through these random-init towers.
+# Used to time the quantised mode (one-term GEMMs on integer codes); parity
+# tests calibrate on their own inputs instead.
+VISION_INPUT_ABSMAX = {"q_proj": 4.79, "k_proj": 4.79, "v_proj": 4.79, "o_proj": 4.59,
+                       "gate_proj": 5.69, "up_proj": 5.69, "down_proj": 13260.0}
+AUDIO_INPUT_ABSMAX = {"ffw_layer_1": 4.68, "ffw_layer_2": 188.8, "q_proj": 5.31, "k_proj": 5.31, "v_proj": 5.31,
+                      "post": 156.6, "linear_start": 6.08, "linear_end": 10.9}
+
+
+def _s_in(s_in, table, name):
+    """s_in: a number (every linear), or "calibrated" (the fixed table above)."""
+    if s_in == "calibrated":
+        return float(np.float32(table[name] / 127.0))
+    return float(s_in)
+
+
+def vision_weights(seed: int = 0, layers: int = VISION_LAYERS, s_in=0.0, s_out: float = 0.0) -> Dict[str, np.ndarray]:
     """Vision tower + embedder with the reference dtypes: I8 QAT linears,
-    BF16 norms / patch projection / position table, F32 embedder."""
+    BF16 norms / patch projection / position table, F32 embedder.  s_in is
+    one input_activation_scale for every linear or "calibrated"."""
     d, ff, hd = VISION_HIDDEN, VISION_FF, VISION_HEAD_DIM
     t: Dict[str, np.ndarray] = {}
     t[VISION_PATCH_PROJ] = _bf16(seed, VISION_PATCH_PROJ, (d, 768), 0.0, 0.02)
@@ -172,10 +191,10 @@ def vision_weights(seed: int = 0, layers: int = VISION_LAYERS, s_in: float = 0.0
     for i in range(layers):
         p = vision_layer_prefix(i)
         for proj in ("q_proj", "k_proj", "v_proj", "o_proj"):
-            _qat_i8(seed, t, f"{p}.self_attn.{proj}.linear", d, d, s_in, s_out)
-        _qat_i8(seed, t, f"{p}.mlp.gate_proj.linear", ff, d, s_in, s_out)
-        _qat_i8(seed, t, f"{p}.mlp.up_proj.linear", ff, d, s_in, s_out)
-        _qat_i8(seed, t, f"{p}.mlp.down_proj.linear", d, ff, s_in, s_out)
+            _qat_i8(seed, t, f"{p}.self_attn.{proj}.linear", d, d, _s_in(s_in, VISION_INPUT_ABSMAX, proj), s_out)
+        _qat_i8(seed, t, f"{p}.mlp.gate_proj.linear", ff, d, _s_in(s_in, VISION_INPUT_ABSMAX, "gate_proj"), s_out)
+        _qat_i8(seed, t, f"{p}.mlp.up_proj.linear", ff, d, _s_in(s_in, VISION_INPUT_ABSMAX, "up_proj"), s_out)
+        _qat_i8(seed, t, f"{p}.mlp.down_proj.linear", d, ff, _s_in(s_in, VISION_INPUT_ABSMAX, "down_proj"), s_out)
         for nm in ("q_norm", "k_norm"):
             name = f"{p}.self_attn.{nm}.weight"
             t[name] = _bf16(seed, name, (hd,), 1.0, 0.02)
@@ -185,9 +204,10 @@ def vision_weights(seed: int = 0, layers: int = VISION_LAYERS, s_in: float = 0.0
     return t
 
 
-def audio_weights(seed: int = 0, layers: int = AUDIO_LAYERS, bits: int = 8, s_in: float = 0.0, s_out: float = 0.0) -> Dict[str, np.ndarray]:
+def audio_weights(seed: int = 0, layers: int = AUDIO_LAYERS, bits: int = 8, s_in=0.0, s_out: float = 0.0) -> Dict[str, np.ndarray]:
     """Audio tower + embedder with the reference dtypes: U8 packed QAT
-    linears (zero point 2**(bits-1)), F32 norms, convs and projections."""
+    linears (zero point 2**(bits-1)), F32 norms, convs and projections.
+    s_in is one input_activation_scale for every linear or "calibrated"."""
     d, ff = AUDIO_HIDDEN, AUDIO_FF
     t: Dict[str, np.ndarray] = {}
     t[f"{AUDIO_SUB}.layer0.conv.weight"] = _f32(seed, f"{AUDIO_SUB}.layer0.conv.weight", (128, 1, 3, 3), 0.0, 0.02)
@@ -201,17 +221,17 @@ def audio_weights(seed: int = 0, layers: int = AUDIO_LAYERS, bits: int = 8, s_in
     for i in range(layers):
         p = audio_layer_prefix(i)
         for blk in ("feed_forward1", "feed_forward2"):
-            _qat_u8(seed, t, f"{p}.{blk}.ffw_layer_1.linear", ff, d, bits, s_in, s_out)
-            _qat_u8(seed, t, f"{p}.{blk}.ffw_layer_2.linear", d, ff, bits, s_in, s_out)
+            _qat_u8(seed, t, f"{p}.{blk}.ffw_layer_1.linear", ff, d, bits, _s_in(s_in, AUDIO_INPUT_ABSMAX, "ffw_layer_1"), s_out)
+            _qat_u8(seed, t, f"{p}.{blk}.ffw_layer_2.linear", d, ff, bits, _s_in(s_in, AUDIO_INPUT_ABSMAX, "ffw_layer_2"), s_out)
             for nm in ("pre_layer_norm", "post_layer_norm"):
                 name = f"{p}.{blk}.{nm}.weight"
                 t[name] = _f32(seed, name, (d,), 1.0, 0.02)
         for proj in ("q_proj", "k_proj", "v_proj", "post"):
-            _qat_u8(seed, t, f"{p}.self_attn.{proj}.linear", d, d, bits, s_in, s_out)
+            _qat_u8(seed, t, f"{p}.self_attn.{proj}.linear", d, d, bits, _s_in(s_in, AUDIO_INPUT_ABSMAX, proj), s_out)
         t[f"{p}.self_attn.per_dim_scale"] = _f32(seed, f"{p}.self_attn.per_dim_scale", (AUDIO_HEAD_DIM,), 0.0, 0.02)
         t[f"{p}.self_attn.relative_k_proj.weight"] = _f32(seed, f"{p}.self_attn.relative_k_proj.weight", (d, d), 0.0, 0.02)
-        _qat_u8(seed, t, f"{p}.lconv1d.linear_start.linear", 2 * d, d, bits, s_in, s_out)
-        _qat_u8(seed, t, f"{p}.lconv1d.linear_end.linear", d, d, bits, s_in, s_out)
+        _qat_u8(seed, t, f"{p}.lconv1d.linear_start.linear", 2 * d, d, bits, _s_in(s_in, AUDIO_INPUT_ABSMAX, "linear_start"), s_out)
+        _qat_u8(seed, t, f"{p}.lconv1d.linear_end.linear", d, d, bits, _s_in(s_in, AUDIO_INPUT_ABSMAX, "linear_end"), s_out)
         for nm in ("pre_layer_norm", "conv_norm"):
             name = f"{p}.lconv1d.{nm}.weight"
             t[name] = _f32(seed, name, (d,), 1.0, 0.02)
