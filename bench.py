@@ -32,6 +32,7 @@ sys.path.insert(0, ROOT)
 PKG = "gemma-4-webgpu-kernels-multimodal_b200"
 
 HIDDEN, FF, HEADS, HD, TEXT = 768, 3072, 12, 64, 1536
+sharding = None  # the package's sharding module, imported with the package
 
 
 def env_int(k, d):
@@ -274,10 +275,7 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     e1.record(stream)
     e1.synchronize()
     launches = native.kernel_launches() - launches0
-    t = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
+    ms = sharding.max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
     audio_seconds = float(lens.sum()) / 16000.0
     value = world * audio_seconds * args.steps / (ms / 1000.0)
     ctx.profile_begin()
@@ -296,9 +294,7 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     t0 = time.perf_counter()
     for _ in range(k_e2e):
         ctx.audio_embed(clips, 16000, 12)
-    te = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    te = sharding.max_over_ranks(time.perf_counter() - t0, dist, "cuda")
     res = {
         "metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": value, "unit": "audio-s/s",
         "ms_per_step": ms / args.steps,
@@ -306,7 +302,7 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
                    "clips_per_gpu": n, "audio_seconds_per_gpu": audio_seconds, "encoder_rows_per_gpu": rows,
                    "activation_quant": QUANT_DESC[args.quant]},
         "gpu_launches": launches,
-        "e2e": {"value": world * audio_seconds * k_e2e / float(te.item()), "unit": "audio-s/s",
+        "e2e": {"value": world * audio_seconds * k_e2e / te, "unit": "audio-s/s",
                 "h2d_bytes_per_step": total * 4, "d2h_bytes_per_step": rows * 1536 * 4},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
                      "frac": ach / peak, "peak_source": "measured (bf16 cuBLAS, sustained)", "traffic": None,
@@ -340,6 +336,8 @@ def run_ours(args):
 
     native = importlib.import_module(PKG + "._native")
     syn = importlib.import_module(PKG + ".synthetic")
+    global sharding
+    sharding = importlib.import_module(PKG + ".sharding")
     B, H, Wd, layers, max_soft = args.batch, 768, 768, 16, 280
     N, tokens = (H // 16) * (Wd // 16), 256
     path = weights_path("vision", layers, args.quant, rank, barrier)
@@ -347,8 +345,8 @@ def run_ours(args):
     ctx.load_weights(path)
 
     pix_host = torch.empty((B, H, Wd, 3), dtype=torch.float32).pin_memory()
-    for i in range(B):
-        pix_host[i] = torch.from_numpy(syn.image_pixels(rank * B + i, H, Wd))
+    for i, seed in enumerate(sharding.image_shard(world * B, world, rank)):  # this rank's images of the job
+        pix_host[i] = torch.from_numpy(syn.image_pixels(seed, H, Wd))
     pix = pix_host.cuda()
     out = torch.empty((B * tokens, TEXT), dtype=torch.float32, device="cuda")
     stream = torch.cuda.Stream()  # a real stream: the library launches on it, the events bracket it
@@ -375,10 +373,7 @@ def run_ours(args):
     ms = e0.elapsed_time(e1)
     barrier()
     clk = clocks.stop()
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = sharding.max_over_ranks(ms, dist, "cuda")
     value = world * B * args.steps / (ms_max / 1000.0)
 
     # roofline of the dominant kernel: per-launch CUDA-event times of one step
@@ -427,10 +422,7 @@ def run_ours(args):
     for _ in range(k_e2e):
         ctx.vision_embed(in_host, max_soft, layers, outs=out_host)
     t_e2e = time.perf_counter() - t0
-    te = torch.tensor([t_e2e], dtype=torch.float64, device="cuda")
-    if dist:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_value = world * B * k_e2e / float(te.item())
+    e2e_value = world * B * k_e2e / sharding.max_over_ranks(t_e2e, dist, "cuda")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
