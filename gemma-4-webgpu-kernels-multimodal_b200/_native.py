@@ -204,15 +204,19 @@ class Context:
         check(lib().g4m_vision_layers(self.h, device, n, height, width, first, count, ptr(h)))
         return h
 
-    def audio_embed(self, clips, sampling_rate=16000, layer_count=12, max_samples=0):
+    def audio_embed(self, clips, sampling_rate=16000, layer_count=12, max_samples=0, outs=None):
+        """clips: list of float32 sample arrays; `outs` optionally supplies
+        C-contiguous float32 output arrays of at least [rows_i, 1536] each."""
         n = len(clips)
         xs = [np.ascontiguousarray(c, dtype=np.float32).reshape(-1) for c in clips]
         lens = np.array([x.size for x in xs], np.int64)
         cap = max_samples if max_samples else 480000
-        outs = []
-        for x in xs:
-            rows = int(lib().g4m_audio_soft_token_count(min(x.size, cap), 320, 160, 750))
-            outs.append(np.zeros((max(rows, 1), 1536), np.float32))
+        need = [int(lib().g4m_audio_soft_token_count(min(x.size, cap), 320, 160, 750)) for x in xs]
+        if outs is None:
+            outs = [np.empty((max(r, 1), 1536), np.float32) for r in need]
+        elif any(o.dtype != np.float32 or not o.flags.c_contiguous or o.ndim != 2 or o.shape[1] != 1536
+                 or o.shape[0] < r for o, r in zip(outs, need)):
+            raise ValueError("outs must be C-contiguous float32 [>= rows, 1536] arrays")
         pin = (ctypes.c_void_p * n)(*[x.ctypes.data for x in xs])
         pout = (ctypes.c_void_p * n)(*[o.ctypes.data for o in outs])
         rows = np.zeros(n, np.int32)
