@@ -303,7 +303,14 @@ cudaError_t audio_subsample(const float* feats, const int* frame_off, const int*
 // 24 (12 past-horizon rows), 13 relative positions, per-dim softplus query
 // scale, tanh softcap.  Out-of-clip context rows add no key term and no
 // value, but their slot stays in the softmax with the relative-only score.
-// One CTA per (clip block of 12 rows, head), 4 warps x 3 query rows.
+// One CTA per (clip block of 12 rows, head), 128 threads:
+//   stage    the 24-row key / value window (keys pre-scaled), the 13
+//            relative keys and the block's 12 scaled queries in shared memory
+//   dots     the 12 x 24 query-key and 12 x 13 query-relative dot products,
+//            each a float4 sequence over the 128 dims, spread over all threads
+//   softmax  one warp per query row, lane = context slot: tanh softcap, max,
+//            exp, sum; weights of out-of-clip slots kept in the denominator
+//   P*V      thread = output dim, 24-term sums for each of the 12 rows
 // qkv: [rows][3 * 1024] f32 (q | k | v); relk: [13][1024]; qmul: [128]
 // (= 128^-0.5 / ln 2 * softplus(per_dim_scale)); kscale = ln(1 + e) / ln 2.
 // ---------------------------------------------------------------------------
@@ -313,77 +320,105 @@ __global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict
                                                          const int* __restrict__ row0, const int* __restrict__ rows,
                                                          float kscale, float softcap, __half* __restrict__ o_hi,
                                                          __half* __restrict__ o_lo, float s_code) {
-  constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, D = 1024;
-  __shared__ float ks[CTX][HD], vs[CTX][HD], rk[PL][HD];
+  constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, D = 1024, PP = HD + 4;  // PP: padded row pitch
+  __shared__ __align__(16) float qs[CH][PP], ks[CTX][PP], rk[PL][PP];
+  __shared__ __align__(16) float vs[CTX][HD];
+  __shared__ float dk[CH][CTX], dr[CH][PL], wt[CH][CTX];
   const int head = blockIdx.y;
   const int clip = blk_clip[blockIdx.x], blk = blk_index[blockIdx.x];
   const long r0 = row0[clip];
   const int nr = rows[clip];
-  const int t = threadIdx.x;
-  for (int i = t; i < CTX * HD; i += 128) {
-    const int c = i / HD, d = i % HD;
-    const int src = blk * CH + c - (CTX - CH);
-    float kv = 0.f, vv = 0.f;
-    if (src >= 0 && src < nr) {
-      const float* row = qkv + (r0 + src) * (3 * D) + head * HD + d;
-      kv = row[D] * kscale;
-      vv = row[2 * D];
+  const int nq = min(CH, nr - blk * CH);  // query rows of this block
+  const int t = threadIdx.x;  // staging: thread = head dim, every row's load in flight at once
+  {
+    const float qm = qmul[t];
+    float kv[CTX], vv[CTX], rv[PL], qv[CH];
+#pragma unroll
+    for (int c = 0; c < CTX; ++c) {
+      const int src = blk * CH + c - (CTX - CH);
+      const bool ok = src >= 0 && src < nr;
+      const float* row = qkv + (r0 + (ok ? src : 0)) * (3 * D) + head * HD + t;
+      kv[c] = ok ? __ldg(row + D) : 0.f;
+      vv[c] = ok ? __ldg(row + 2 * D) : 0.f;
     }
-    ks[c][d] = kv;
-    vs[c][d] = vv;
+#pragma unroll
+    for (int r = 0; r < PL; ++r) rv[r] = __ldg(relk + r * D + head * HD + t);
+#pragma unroll
+    for (int qi = 0; qi < CH; ++qi)
+      qv[qi] = qi < nq ? __ldg(qkv + (r0 + blk * CH + qi) * (3 * D) + head * HD + t) : 0.f;
+#pragma unroll
+    for (int c = 0; c < CTX; ++c) {
+      ks[c][t] = kv[c] * kscale;
+      vs[c][t] = vv[c];
+    }
+#pragma unroll
+    for (int r = 0; r < PL; ++r) rk[r][t] = rv[r];
+#pragma unroll
+    for (int qi = 0; qi < CH; ++qi) qs[qi][t] = qv[qi] * qm;
   }
-  for (int i = t; i < PL * HD; i += 128) rk[i / HD][i % HD] = relk[(i / HD) * D + head * HD + (i % HD)];
+  __syncthreads();
+  // dot products: items [0, 288) query-key, [288, 444) query-relative
+  for (int it = t; it < CH * CTX + CH * PL; it += 128) {
+    const bool isk = it < CH * CTX;
+    const int qi = isk ? it / CTX : (it - CH * CTX) / PL;
+    const int c = isk ? it % CTX : (it - CH * CTX) % PL;
+    if (qi >= nq) continue;
+    const float4* a = reinterpret_cast<const float4*>(qs[qi]);
+    const float4* b = reinterpret_cast<const float4*>(isk ? ks[c] : rk[c]);
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // four independent chains
+#pragma unroll 8
+    for (int j = 0; j < HD / 4; ++j) {
+      const float4 x = a[j], y = b[j];
+      s0 = fmaf(x.x, y.x, s0);
+      s1 = fmaf(x.y, y.y, s1);
+      s2 = fmaf(x.z, y.z, s2);
+      s3 = fmaf(x.w, y.w, s3);
+    }
+    const float s = (s0 + s1) + (s2 + s3);
+    if (isk) dk[qi][c] = s;
+    else dr[qi][c] = s;
+  }
+  for (int i = t; i < CH * CTX; i += 128) wt[i / CTX][i % CTX] = 0.f;
   __syncthreads();
   const int lane = t & 31, warp = t >> 5;
-  float qm[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) qm[j] = qmul[lane + 32 * j];
-  for (int qi = warp; qi < CH; qi += 4) {
-    const int lr = blk * CH + qi;  // local query row
-    if (lr >= nr) break;
-    const float* qrow = qkv + (r0 + lr) * (3 * D) + head * HD;
-    float q[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) q[j] = qrow[lane + 32 * j] * qm[j];
-    float myscore = -INFINITY;  // lane c < 24 keeps score of context c
-    for (int c = 0; c < CTX; ++c) {
-      const int src = blk * CH + c - (CTX - CH);
-      const int rel = c - qi;
-      const bool kv_ok = src >= 0 && src < nr;
-      const bool rel_ok = rel >= 0 && rel < PL;
-      float p = 0.f;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float kk = (kv_ok ? ks[c][lane + 32 * j] : 0.f) + (rel_ok ? rk[rel][lane + 32 * j] : 0.f);
-        p = fmaf(q[j], kk, p);
-      }
-      p = warp_sum_a(p);
-      const float sc = tanhf(p / softcap) * softcap;
-      if (lane == c) myscore = sc;
+  for (int qi = warp; qi < nq; qi += 4) {
+    const int src = blk * CH + lane - (CTX - CH);
+    const bool kv_ok = lane < CTX && src >= 0 && src < nr;
+    const int rel = lane - qi;
+    const bool rel_ok = lane < CTX && rel >= 0 && rel < PL;
+    float sc = -INFINITY;
+    if (lane < CTX) {
+      const float p = (kv_ok ? dk[qi][lane] : 0.f) + (rel_ok ? dr[qi][rel] : 0.f);
+      sc = tanhf(p / softcap) * softcap;
     }
-    const float mx = warp_max_a(myscore);
-    const float e = lane < CTX ? expf(myscore - mx) : 0.f;
+    const float mx = warp_max_a(sc);
+    const float e = lane < CTX ? expf(sc - mx) : 0.f;
     const float den = warp_sum_a(e);
-    const float w = e / den;
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < CTX; ++c) {
-      const float wc = __shfl_sync(0xffffffffu, w, c);
-      const int src = blk * CH + c - (CTX - CH);
-      if (src < 0 || src >= nr) continue;
+    if (lane < CTX) wt[qi][lane] = kv_ok ? e / den : 0.f;  // out-of-clip slots add no value
+  }
+  __syncthreads();
+  const float inv_code = s_code != 0.0f ? 1.0f / s_code : 0.0f;
+  float acc[CH];  // the 12 rows' sums as independent chains (rows >= nq have zero weights)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) o[j] = fmaf(wc, vs[c][lane + 32 * j], o[j]);
-    }
-    const long orow = r0 + lr;
+  for (int qi = 0; qi < CH; ++qi) acc[qi] = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (s_code != 0.0f) {  // integer codes for the post projection's input scale
-        o_hi[orow * D + head * HD + lane + 32 * j] = __float2half_rn(srq_code(o[j], s_code, 1.0f / s_code));
-      } else {
-        __half h, l;
-        split_f16(o[j], h, l);
-        o_hi[orow * D + head * HD + lane + 32 * j] = h;
-        o_lo[orow * D + head * HD + lane + 32 * j] = l;
-      }
+  for (int c = 0; c < CTX; ++c) {
+    const float v = vs[c][t];
+#pragma unroll
+    for (int qi = 0; qi < CH; ++qi) acc[qi] = fmaf(wt[qi][c], v, acc[qi]);
+  }
+#pragma unroll
+  for (int qi = 0; qi < CH; ++qi) {
+    if (qi >= nq) break;
+    const float o = acc[qi];
+    const long oi = (r0 + blk * CH + qi) * D + head * HD + t;
+    if (s_code != 0.0f) {  // integer codes for the post projection's input scale
+      o_hi[oi] = __float2half_rn(srq_code(o, s_code, inv_code));
+    } else {
+      __half h, l;
+      split_f16(o, h, l);
+      o_hi[oi] = h;
+      o_lo[oi] = l;
     }
   }
 }
