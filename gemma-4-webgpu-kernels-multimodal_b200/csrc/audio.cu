@@ -243,7 +243,13 @@ int load_audio(Device& d, const SafeTensors& f) {
     if (!t6) return rc;
     L.n_lpre = up(d, t1, f);
     L.n_conv = up(d, t2, f);
-    L.dw = up(d, t3, f);
+    {  // depthwise weights transposed to [5][1024] (four channels per vector load)
+      const float* w = (const float*)f.data(*t3);
+      std::vector<float> wt(5 * D);
+      for (int c = 0; c < D; ++c)
+        for (int k = 0; k < 5; ++k) wt[k * D + c] = w[c * 5 + k];
+      L.dw = upload_f32(d, wt.data(), wt.size());
+    }
     L.n_pre_attn = up(d, t4, f);
     L.n_post_attn = up(d, t5, f);
     L.n_out = up(d, t6, f);
@@ -291,8 +297,24 @@ static int ensure_mel(Device& d, int sr) {
       filt[(size_t)b * nmel + m] = (float)std::max(0.0, std::min(u, dn));
     }
   }
+  // non-zero bin range of every channel: the device sums only those terms, in
+  // bin order, which leaves each double sum bit-identical to the dense one
+  std::vector<int> rng(2 * nmel);
+  for (int m = 0; m < nmel; ++m) {
+    int lo = bins, hi = -1;
+    for (int b = 0; b < bins; ++b)
+      if (filt[(size_t)b * nmel + m] != 0.0f) {
+        lo = std::min(lo, b);
+        hi = b;
+      }
+    rng[2 * m] = lo;
+    rng[2 * m + 1] = hi;  // empty channel: lo > hi
+  }
   if (!d.aw.mel) d.aw.mel = (float*)dalloc(d, filt.size() * 4);
-  if (!d.aw.mel || cudaMemcpy(d.aw.mel, filt.data(), filt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+  if (!d.aw.mel_rng) d.aw.mel_rng = (int*)dalloc(d, rng.size() * 4);
+  if (!d.aw.mel || !d.aw.mel_rng ||
+      cudaMemcpy(d.aw.mel, filt.data(), filt.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(d.aw.mel_rng, rng.data(), rng.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
     return fail(G4M_E_CUDA, "mel filter upload failed");
   d.aw_mel_sr = sr;
   return G4M_OK;
@@ -590,7 +612,7 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   float* h = (float*)b.h.p;
   // front end (preprocessGemma4AudioSamples + runAudioSubsampleProjectionCpu)
   G4M_RUN("logmel", audio_logmel(samples_dev, (const long*)b.sample_off.p, (const long*)b.sample_len.p, dfoff, dfcnt, n,
-                                 (int)FR, aw.window, aw.mel, aw.twiddle, (float*)b.feats.p, nullptr, st));
+                                 (int)FR, aw.window, aw.mel, aw.mel_rng, aw.twiddle, (float*)b.feats.p, st));
   const int max_rows = *std::max_element(rows.begin(), rows.end());
   G4M_RUN("subsample", audio_subsample((const float*)b.feats.p, dfoff, dfcnt, (const int*)b.t0_off.p,
                                        (const int*)b.clip_row0.p, (const int*)b.clip_rows.p, n, max_t0, max_rows,

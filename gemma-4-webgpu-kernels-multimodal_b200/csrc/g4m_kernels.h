@@ -129,9 +129,10 @@ cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __
                                 __half* o_hi, __half* o_lo, float s_code, int* err, cudaStream_t st);
 
 // Audio helpers -- kernels_audio.cu
+// mel_rng: [128][2] first / last non-zero FFT bin of each mel channel.
 cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
                          const int* frames, int clips, int total_frames, const float* window, const float* mel,
-                         const double2* twiddle, float* features, uint8_t* mask, cudaStream_t st);
+                         const int* mel_rng, const double2* twiddle, float* features, cudaStream_t st);
 // Layer-0 rows of clip i start at packed layer-0 row t0off[i] of l0 (scratch
 // [sum T0][64][128] f32); output rows at packed row row0[i], rows[i] of them.
 cudaError_t audio_subsample(const float* feats, const int* frame_off, const int* frames, const int* t0off,

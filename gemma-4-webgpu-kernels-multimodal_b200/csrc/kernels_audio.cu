@@ -32,7 +32,8 @@ __global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ s
                                                      const long* __restrict__ slen, const int* __restrict__ foff,
                                                      const int* __restrict__ fcount, int clips,
                                                      const float* __restrict__ window, const float* __restrict__ mel,
-                                                     const double2* __restrict__ tw, float* __restrict__ feats) {
+                                                     const int* __restrict__ mel_rng, const double2* __restrict__ tw,
+                                                     float* __restrict__ feats) {
   __shared__ float re[512], im[512], mag[257];
   const int gf = blockIdx.x;
   // clip of this frame: binary search over frame offsets
@@ -78,19 +79,19 @@ __global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ s
   for (int b = t; b < 257; b += 256) mag[b] = (float)hypot((double)re[b], (double)im[b]);
   __syncthreads();
   if (t < 128) {
-    double e = 0.0;  // mel energy in double (JS number), in bin order
-    for (int b = 0; b < 257; ++b) e += (double)mag[b] * (double)mel[b * 128 + t];
+    double e = 0.0;  // mel energy in double (JS number), in bin order, over the non-zero bins
+    const int b1 = mel_rng[2 * t + 1];
+    for (int b = mel_rng[2 * t]; b <= b1; ++b) e += (double)mag[b] * (double)mel[b * 128 + t];
     feats[(long)gf * 128 + t] = (float)log(e + 0.001);
   }
 }
 
 cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
                          const int* frames, int clips, int total_frames, const float* window, const float* mel,
-                         const double2* twiddle, float* features, uint8_t* mask, cudaStream_t st) {
-  (void)mask;
+                         const int* mel_rng, const double2* twiddle, float* features, cudaStream_t st) {
   if (total_frames <= 0) return cudaSuccess;
   logmel_kernel<<<total_frames, 256, 0, st>>>(samples, sample_off, sample_len, frame_off, frames, clips, window, mel,
-                                              twiddle, features);
+                                              mel_rng, twiddle, features);
   return cudaGetLastError();
 }
 
@@ -438,7 +439,7 @@ cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const fl
 // clip (runAudioDepthwiseCausalConv1dCpu, src/audio/kernels.ts:855-884),
 // conv_norm RMSNorm, SiLU (runSiluActivationCpu) -> fp16 hi/lo operand of
 // linear_end (integer codes when s_code, linear_end's input scale, is non-zero).
-// One warp per row, d = 1024.  dw: [1024][5].
+// One warp per row, d = 1024.  dw: [5][1024] (tap-major).
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) lconv_kernel(const float* __restrict__ g, const float* __restrict__ dw,
                                                     const float* __restrict__ nw, const int* __restrict__ row_clip,
@@ -458,14 +459,15 @@ __global__ void __launch_bounds__(256) lconv_kernel(const float* __restrict__ g,
     const long src = local + k - (KS - 1);
     if (src < 0) continue;
     const float4* x = reinterpret_cast<const float4*>(g + (row + k - (KS - 1)) * D);
+    const float4* wk = reinterpret_cast<const float4*>(dw + k * D);
 #pragma unroll
     for (int i = 0; i < V; ++i) {
-      const int c = 4 * (lane + 32 * i);
       const float4 v = x[lane + 32 * i];
-      acc[i].x = fmaf(v.x, dw[(c + 0) * KS + k], acc[i].x);
-      acc[i].y = fmaf(v.y, dw[(c + 1) * KS + k], acc[i].y);
-      acc[i].z = fmaf(v.z, dw[(c + 2) * KS + k], acc[i].z);
-      acc[i].w = fmaf(v.w, dw[(c + 3) * KS + k], acc[i].w);
+      const float4 w = __ldg(wk + lane + 32 * i);
+      acc[i].x = fmaf(v.x, w.x, acc[i].x);
+      acc[i].y = fmaf(v.y, w.y, acc[i].y);
+      acc[i].z = fmaf(v.z, w.z, acc[i].z);
+      acc[i].w = fmaf(v.w, w.w, acc[i].w);
     }
   }
   float ss = 0.f;

@@ -89,6 +89,7 @@ struct AudioWeights {
   __half *emb_hi = nullptr, *emb_lo = nullptr;  // embedder [1536, 1536]
   float* window = nullptr;   // periodic Hann [320]
   float* mel = nullptr;      // [257][128]
+  int* mel_rng = nullptr;    // [128][2] first / last FFT bin with a non-zero weight per mel channel
   double2* twiddle = nullptr;  // [256] exp(-2 pi i k / 512)
 };
 
