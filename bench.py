@@ -326,6 +326,48 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     return res
 
 
+def qat_sweep(native, syn, peak, steps=10):
+    """The cfg0 int8 QAT linear (768 -> 768, per-channel scales, bias) on
+    device-resident activations at M = 256 (cfg0 itself), 18432 (8 images)
+    and 147456 (64 images): per-launch CUDA-event time of the tensor-core
+    GEMM, algorithmic TFLOP/s and the fraction of the measured peak."""
+    import ctypes
+    import torch
+    L = native.lib()
+    ctx = native.Context([torch.cuda.current_device()])
+    out = {}
+    try:
+        _, w, s, b = syn.qat_linear_case(0, rows=1)
+        h = ctypes.c_void_p()
+        native.check(L.g4m_linear_prepare(ctx.h, 0, native.ptr(w), 0, 768, 768, native.ptr(s), 0.0, 0.0,
+                                          native.ptr(b), ctypes.byref(h)))
+        try:
+            for M in (256, 18432, 147456):
+                x = torch.randn((M, 768), dtype=torch.float32, device="cuda")
+                y = torch.empty((M, 768), dtype=torch.float32, device="cuda")
+                st = torch.cuda.current_stream().cuda_stream
+                run = lambda: native.check(L.g4m_linear_run(h, ctypes.c_void_p(x.data_ptr()), M,
+                                                            ctypes.c_void_p(y.data_ptr()), ctypes.c_void_p(st)))
+                for _ in range(3):
+                    run()
+                torch.cuda.synchronize()
+                ctx.profile_begin()
+                for _ in range(steps):
+                    run()
+                prof = ctx.profile_end()
+                cnt, tot = prof["gemm_qat"]
+                ms = tot / cnt
+                tf = 2.0 * M * 768 * 768 / (ms / 1000.0) / 1e12
+                out[str(M)] = {"gemm_ms": round(ms, 5), "tflops": round(tf, 1), "frac": round(tf / peak, 4),
+                               "operand_ms": round(prof["prep_a"][1] / prof["prep_a"][0], 5)}
+        finally:
+            L.g4m_linear_free(h)
+    finally:
+        ctx.close()
+    return {"workload": "int8 QAT linear 768x768 (+bias), activations resident; algorithmic 2*M*768*768",
+            "peak": peak, "by_rows": out}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -439,6 +481,7 @@ def run_ours(args):
         s, desc = cpu_vision_sample(threads, args.quant)
         cpu = {"value": 1.0 / s, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc}
 
+    sweep = qat_sweep(native, syn, peak) if rank == 0 else None
     audio = None
     if not args.no_audio:
         ctx.close()
@@ -461,6 +504,7 @@ def run_ours(args):
             "gpu_launches": launches,
             "roofline": roofline,
             "qat_linear": qat_linear,
+            "qat_linear_sweep": sweep,
             "kernel_ms_per_step": kernel_ms,
             "cpu_baseline": cpu,
             "clocks": clk,

@@ -104,10 +104,11 @@ def _rounded_sample(v: np.ndarray) -> List[float]:
 # ---------------------------------------------------------------------------
 
 def preprocessGemma4ImageBlob(blob: Dict, options: Optional[Dict] = None) -> Dict:
-    """blob = {"pixels": uint8 [h, w, 3|4] or float32 [h, w, 3] in [0, 1],
-    "width", "height"}.  The pixels must already be at the token layout's
-    target size (the reference's browser-canvas resampling is not
-    reproducible off-browser)."""
+    """blob = {"pixels": uint8 [h, w, 3|4] of any size, or float32 [h, w, 3]
+    in [0, 1] already at the token layout's target size; "width", "height"}.
+    uint8 images off the target size are resized on the GPU (g4m_resize_rgb:
+    antialiased linear filter, 8-bit rounding, 1/255 rescale) in place of the
+    reference's browser-canvas drawImage, whose smoothing is unspecified."""
     o = options or {}
     patch = o.get("patchSize", 16)
     max_soft = o.get("maxSoftTokens", 280)
@@ -117,11 +118,14 @@ def preprocessGemma4ImageBlob(blob: Dict, options: Optional[Dict] = None) -> Dic
     h, w = int(blob.get("height", px.shape[0])), int(blob.get("width", px.shape[1]))
     layout = computeGemma4ImageTokenLayout({"height": h, "width": w, "patchSize": patch, "maxSoftTokens": max_soft,
                                             "poolingKernelSize": pool})
-    if layout["target"]["height"] != h or layout["target"]["width"] != w:
-        raise ValueError(f"pixels must already be at the token layout's target size "
-                         f"{layout['target']['height']} x {layout['target']['width']}")
-    rgb = (px[..., :3].astype(np.float64) * rescale).astype(np.float32) if px.dtype == np.uint8 else \
-        np.ascontiguousarray(px[..., :3], dtype=np.float32)
+    th, tw = layout["target"]["height"], layout["target"]["width"]
+    if (th, tw) != (h, w):
+        if px.dtype != np.uint8 or rescale != 1 / 255:
+            raise ValueError(f"float pixels must already be at the token layout's target size {th} x {tw}")
+        rgb = context().resize_rgb(px, th, tw)
+    else:
+        rgb = (px[..., :3].astype(np.float64) * rescale).astype(np.float32) if px.dtype == np.uint8 else \
+            np.ascontiguousarray(px[..., :3], dtype=np.float32)
     gh, gw = layout["patchGrid"]["height"], layout["patchGrid"]["width"]
     pp = patch * patch * 3
     pv = np.zeros((layout["maxPatches"], pp), np.float32)
@@ -147,13 +151,16 @@ def _vision_failure(started, layer_count, err) -> Dict:
 
 
 def computeGemma4VisionImageEmbeddingsBatch(inputs: List[Dict]) -> List[Dict]:
-    """Batched computeGemma4VisionImageEmbeddings: images of one size in one
-    call, sharded across the configured GPUs."""
+    """Batched computeGemma4VisionImageEmbeddings, sharded across the
+    configured GPUs.  uint8 images may have any sizes (resized on the GPU,
+    grouped by token layout); float32 pixels must share one target size."""
     started = time.perf_counter()
     if not inputs:
         return []
     layer_count = inputs[0].get("layerCount", VISION_ENCODER_LAYER_COUNT)
     max_soft = inputs[0].get("maxSoftTokens", 280)
+    if all(np.asarray(i["blob"]["pixels"]).dtype == np.uint8 for i in inputs):
+        return _vision_images(inputs, layer_count, max_soft, started)
     try:
         if not isinstance(layer_count, int) or layer_count < 1 or layer_count > VISION_ENCODER_LAYER_COUNT:
             raise ValueError(f"Vision encoder layer count must be 1-{VISION_ENCODER_LAYER_COUNT}, got {layer_count}.")
@@ -172,6 +179,31 @@ def computeGemma4VisionImageEmbeddingsBatch(inputs: List[Dict]) -> List[Dict]:
                     "layout": p["layout"], "layerCount": layer_count, "rows": int(r), "dim": 1536,
                     "embeddings": e.reshape(-1), "finite": finite, "checksum": checksumFloats(e),
                     "firstValues": _rounded_sample(e)})
+    return res
+
+
+def _vision_images(inputs, layer_count, max_soft, started) -> List[Dict]:
+    """Decoded 8-bit images of any sizes through g4m_vision_embed_images."""
+    try:
+        if not isinstance(layer_count, int) or layer_count < 1 or layer_count > VISION_ENCODER_LAYER_COUNT:
+            raise ValueError(f"Vision encoder layer count must be 1-{VISION_ENCODER_LAYER_COUNT}, got {layer_count}.")
+        imgs = [np.asarray(i["blob"]["pixels"]) for i in inputs]
+        outs, rows, status = context().vision_embed_images(imgs, max_soft, layer_count)
+    except Exception as e:  # never raise, as the reference
+        return [_vision_failure(started, layer_count, e) for _ in inputs]
+    ms = round((time.perf_counter() - started) * 1000)
+    res = []
+    for im, e, r, st in zip(imgs, outs, rows, status):
+        if st != 0:
+            res.append(_vision_failure(started, layer_count, f"{_native.STATUS_NAMES.get(int(st), st)}"))
+            continue
+        lay = computeGemma4ImageTokenLayout({"height": im.shape[0], "width": im.shape[1], "patchSize": 16,
+                                             "maxSoftTokens": max_soft, "poolingKernelSize": 3})
+        finite = bool(np.isfinite(e).all())
+        res.append({"ok": finite, "modelId": GEMMA4_MEDIA_MODEL_ID, "durationMs": ms,
+                    "source": {"width": int(im.shape[1]), "height": int(im.shape[0])}, "layout": lay,
+                    "layerCount": layer_count, "rows": int(r), "dim": 1536, "embeddings": e.reshape(-1),
+                    "finite": finite, "checksum": checksumFloats(e), "firstValues": _rounded_sample(e)})
     return res
 
 

@@ -37,6 +37,8 @@ _SIGS = [
     ("g4m_linear_run", _I, [_VP, _VP, _I, _VP, _VP]),
     ("g4m_linear_free", None, [_VP]),
     ("g4m_linear_run_noalloc", _I, [_VP, _VP, _I, _VP, _VP]),
+    ("g4m_vision_embed_images", _I, [_VP, _I, _VP, _VP, _VP, _I, _I, _I, _VP, _VP, _VP]),
+    ("g4m_resize_rgb", _I, [_VP, _I, _VP, _I, _I, _I, _I, _I, _VP]),
     ("g4m_vision_embed_batch", _I, [_VP, _I, _VP, _I, _I, _I, _I, _VP, _VP, _VP]),
     ("g4m_vision_embed_device", _I, [_VP, _I, _I, _VP, _I, _I, _I, _I, _VP, _VP]),
     ("g4m_vision_debug_hidden", _I, [_VP, _I, _I, _VP, ctypes.c_size_t]),
@@ -188,6 +190,42 @@ class Context:
                                           ctypes.cast(pout, ctypes.c_void_p), ptr(rows), ptr(status))
         check(rc)
         return outs, rows
+
+    def vision_embed_images(self, images, max_soft_tokens=280, layer_count=16):
+        """images: list of uint8 [h, w, 3 | 4] arrays of any sizes (one channel
+        count).  Returns ([tokens_i, 1536] float32 arrays, rows, statuses);
+        per-image failures are reported in the statuses, not raised."""
+        n = len(images)
+        if n == 0:
+            return [], np.zeros(0, np.int32), np.zeros(0, np.int32)
+        imgs = [np.ascontiguousarray(im, dtype=np.uint8) for im in images]
+        ch = imgs[0].shape[2]
+        if any(im.ndim != 3 or im.shape[2] != ch for im in imgs):
+            raise ValueError("images must be [h, w, c] uint8 with one channel count")
+        hs = np.array([im.shape[0] for im in imgs], np.int32)
+        ws = np.array([im.shape[1] for im in imgs], np.int32)
+        outs = []
+        for im in imgs:
+            lay = (ctypes.c_int64 * 6)()
+            rc = lib().g4m_image_token_layout(im.shape[0], im.shape[1], 16, max_soft_tokens, 3, lay)
+            outs.append(np.empty((max(int(lay[5]), 1) if rc == 0 else 1, 1536), np.float32))
+        pin = (ctypes.c_void_p * n)(*[im.ctypes.data for im in imgs])
+        pout = (ctypes.c_void_p * n)(*[o.ctypes.data for o in outs])
+        rows = np.zeros(n, np.int32)
+        status = np.zeros(n, np.int32)
+        rc = lib().g4m_vision_embed_images(self.h, n, ctypes.cast(pin, ctypes.c_void_p), ptr(hs), ptr(ws), ch,
+                                           max_soft_tokens, layer_count, ctypes.cast(pout, ctypes.c_void_p),
+                                           ptr(rows), ptr(status))
+        if rc and not (status != 0).any():
+            check(rc)
+        return [o[: int(r)] for o, r in zip(outs, rows)], rows, status
+
+    def resize_rgb(self, image, target_height: int, target_width: int, device=0) -> np.ndarray:
+        im = np.ascontiguousarray(image, dtype=np.uint8)
+        out = np.empty((target_height, target_width, 3), np.float32)
+        check(lib().g4m_resize_rgb(self.h, device, ptr(im), im.shape[0], im.shape[1], im.shape[2], target_height,
+                                   target_width, ptr(out)))
+        return out
 
     def vision_embed_device(self, pixels_ptr: int, n: int, height: int, width: int, out_ptr: int, max_soft_tokens=280,
                             layer_count=16, stream: int = 0, device=0) -> None:

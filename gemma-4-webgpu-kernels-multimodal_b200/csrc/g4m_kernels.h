@@ -120,6 +120,10 @@ cudaError_t vision_patch_operand(const float* pixels, int n_images, int height, 
                                  __half* lo, cudaStream_t st);
 cudaError_t vision_pool_operand(const float* h, const int* pool_idx, int n_images, int rows_per_image, int tokens,
                                 int k2, int d, float eps, float* pooled_out, __half* hi, __half* lo, cudaStream_t st);
+// RGB(A) uint8 [h][w][c] (c = 3 or 4) -> [th][tw][3] f32 in [0, 1]: antialiased
+// linear resize, 8-bit rounding, 1/255 rescale.  tmp: [h][tw][3] f32.
+cudaError_t vision_resize(const uint8_t* src, int h, int w, int c, int th, int tw, float* tmp, float* dst,
+                          cudaStream_t st);
 // s_code != 0: O is stored as integer codes for the o_proj input scale (o_hi only).
 cudaError_t vision_attention_simt(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
                                   const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,

@@ -196,3 +196,80 @@ cudaError_t vision_attention_simt(const __half* q_hi, const __half* q_lo, const 
 }
 
 }  // namespace g4m
+
+namespace g4m {
+
+// ---------------------------------------------------------------------------
+// Image resize to the token layout's target size (the canvas drawImage step
+// of preprocessGemma4ImageSource, src/preprocess/image.ts:121-128).  The
+// browser's "high quality" smoothing is not specified, so this is the
+// separable antialiased linear (triangle) filter of PIL / torchvision:
+// for output index i of an axis scaled by s = in / out, centre (i + 0.5) s,
+// radius r = max(s, 1), weights max(0, 1 - |x + 0.5 - centre| / r) over the
+// source pixels x in range, normalised.  At s = 1 it is the identity.  The
+// result is rounded to 8 bits (the canvas stores RGBA8) and rescaled by 1/255
+// as the reference does.  Pass 1 filters rows ([h][w][c] uint8 ->
+// [h][tw][3] f32), pass 2 columns (-> [th][tw][3] f32 in [0, 1]).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float tri_weight(float x, float centre, float radius) {
+  return fmaxf(0.f, 1.f - fabsf(x + 0.5f - centre) / radius);
+}
+
+__global__ void resize_rows_kernel(const uint8_t* __restrict__ src, int h, int w, int c, int tw,
+                                   float* __restrict__ tmp) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)h * tw) return;
+  const int y = (int)(i / tw), ox = (int)(i % tw);
+  const float s = (float)w / (float)tw, r = fmaxf(s, 1.f), centre = (ox + 0.5f) * s;
+  const int x0 = max(0, (int)floorf(centre - r)), x1 = min(w - 1, (int)ceilf(centre + r));
+  float acc[3] = {0.f, 0.f, 0.f}, ws = 0.f;
+  for (int x = x0; x <= x1; ++x) {
+    const float wt = tri_weight((float)x, centre, r);
+    if (wt == 0.f) continue;
+    const uint8_t* p = src + ((long)y * w + x) * c;
+    acc[0] = fmaf(wt, (float)p[0], acc[0]);
+    acc[1] = fmaf(wt, (float)p[1], acc[1]);
+    acc[2] = fmaf(wt, (float)p[2], acc[2]);
+    ws += wt;
+  }
+  const float inv = ws > 0.f ? 1.f / ws : 0.f;
+  float* o = tmp + i * 3;
+  o[0] = acc[0] * inv;
+  o[1] = acc[1] * inv;
+  o[2] = acc[2] * inv;
+}
+
+__global__ void resize_cols_kernel(const float* __restrict__ tmp, int h, int tw, int th, float* __restrict__ dst) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)th * tw) return;
+  const int oy = (int)(i / tw), ox = (int)(i % tw);
+  const float s = (float)h / (float)th, r = fmaxf(s, 1.f), centre = (oy + 0.5f) * s;
+  const int y0 = max(0, (int)floorf(centre - r)), y1 = min(h - 1, (int)ceilf(centre + r));
+  float acc[3] = {0.f, 0.f, 0.f}, ws = 0.f;
+  for (int y = y0; y <= y1; ++y) {
+    const float wt = tri_weight((float)y, centre, r);
+    if (wt == 0.f) continue;
+    const float* p = tmp + ((long)y * tw + ox) * 3;
+    acc[0] = fmaf(wt, p[0], acc[0]);
+    acc[1] = fmaf(wt, p[1], acc[1]);
+    acc[2] = fmaf(wt, p[2], acc[2]);
+    ws += wt;
+  }
+  const float inv = ws > 0.f ? 1.f / ws : 0.f;
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    const float q = fminf(fmaxf(floorf(acc[k] * inv + 0.5f), 0.f), 255.f);  // RGBA8 canvas value
+    dst[i * 3 + k] = (float)((double)q * (1.0 / 255.0));  // imageData * rescaleFactor, Float32Array store
+  }
+}
+
+cudaError_t vision_resize(const uint8_t* src, int h, int w, int c, int th, int tw, float* tmp, float* dst,
+                          cudaStream_t st) {
+  if (h <= 0 || w <= 0 || th <= 0 || tw <= 0 || (c != 3 && c != 4)) return cudaErrorInvalidValue;
+  const long n1 = (long)h * tw, n2 = (long)th * tw;
+  resize_rows_kernel<<<(unsigned)((n1 + 255) / 256), 256, 0, st>>>(src, h, w, c, tw, tmp);
+  resize_cols_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(tmp, h, tw, th, dst);
+  return cudaGetLastError();
+}
+
+}  // namespace g4m

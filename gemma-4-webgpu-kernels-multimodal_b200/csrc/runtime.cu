@@ -9,6 +9,7 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -882,6 +883,114 @@ int g4m_vision_embed_batch(g4m_ctx* ctx, int n, const float* const* pixels, int 
     if (rcs[g] && !first) {
       first = rcs[g];
       tl_err = msgs[g];
+    }
+  }
+  return first;
+}
+
+int g4m_resize_rgb(g4m_ctx* ctx, int di, const uint8_t* src, int height, int width, int channels, int target_height,
+                   int target_width, float* dst) {
+  if (!ctx || di < 0 || di >= (int)ctx->devs.size() || !src || !dst || height <= 0 || width <= 0 ||
+      target_height <= 0 || target_width <= 0 || (channels != 3 && channels != 4))
+    return fail(G4M_E_ARG, "bad argument");
+  Device& d = *ctx->devs[di];
+  std::lock_guard<std::mutex> lk(d.mu);
+  cudaSetDevice(d.id);
+  (void)cudaGetLastError();
+  const size_t nsrc = (size_t)height * width * channels, ntmp = (size_t)height * target_width * 3,
+               ndst = (size_t)target_height * target_width * 3;
+  if (ensure(d.io_src, nsrc) || ensure(d.io_tmp, ntmp * 4) || ensure(d.io_out, ndst * 4))
+    return fail(G4M_E_CUDA, "resize buffer allocation failed");
+  G4M_LAUNCH(cudaMemcpyAsync(d.io_src.p, src, nsrc, cudaMemcpyHostToDevice, d.st));
+  cudaStream_t st = d.st;
+  G4M_RUN("resize", vision_resize((const uint8_t*)d.io_src.p, height, width, channels, target_height, target_width,
+                                  (float*)d.io_tmp.p, (float*)d.io_out.p, st));
+  G4M_LAUNCH(cudaMemcpyAsync(dst, d.io_out.p, ndst * 4, cudaMemcpyDeviceToHost, d.st));
+  return finish(d, d.st);
+}
+
+int g4m_vision_embed_images(g4m_ctx* ctx, int n, const uint8_t* const* images, const int* heights, const int* widths,
+                            int channels, int max_soft_tokens, int layer_count, float* const* out, int* rows_out,
+                            int* status) {
+  if (!ctx || n < 0 || (n > 0 && (!images || !heights || !widths || !out))) return fail(G4M_E_ARG, "bad argument");
+  if (channels != 3 && channels != 4) return fail(G4M_E_ARG, "channels must be 3 (RGB) or 4 (RGBA)");
+  // token layout of every image (computeGemma4ImageTokenLayout), grouped by target size
+  std::vector<int64_t> lay((size_t)n * 6);
+  std::vector<int> rcs(n, G4M_OK);
+  std::vector<std::string> msgs(n);
+  std::vector<std::pair<long, int>> keyed;
+  for (int i = 0; i < n; ++i) {
+    if (rows_out) rows_out[i] = 0;
+    rcs[i] = image_layout(heights[i], widths[i], 16, max_soft_tokens, 3, &lay[(size_t)i * 6]);
+    if (rcs[i]) msgs[i] = tl_err;
+    else keyed.push_back({lay[(size_t)i * 6] * 100000L + lay[(size_t)i * 6 + 1], i});
+  }
+  std::stable_sort(keyed.begin(), keyed.end());
+  const int G = (int)ctx->devs.size();
+  for (size_t a = 0; a < keyed.size();) {
+    size_t b = a;
+    while (b < keyed.size() && keyed[b].first == keyed[a].first) ++b;
+    std::vector<int> grp;
+    for (size_t k = a; k < b; ++k) grp.push_back(keyed[k].second);
+    a = b;
+    const int th = (int)lay[(size_t)grp[0] * 6], tw = (int)lay[(size_t)grp[0] * 6 + 1];
+    const int tokens = (int)lay[(size_t)grp[0] * 6 + 5];
+    const int m = (int)grp.size();
+    auto work = [&](int g) {
+      const int lo = (int)((long)m * g / G), hi = (int)((long)m * (g + 1) / G), cnt = hi - lo;
+      if (cnt <= 0) return;
+      Device& d = *ctx->devs[g];
+      std::lock_guard<std::mutex> lk(d.mu);
+      cudaSetDevice(d.id);
+      (void)cudaGetLastError();
+      const size_t img = (size_t)th * tw * 3, ob = (size_t)tokens * 1536;
+      size_t src_total = 0, tmp_max = 0;
+      for (int k = lo; k < hi; ++k) {
+        const int i = grp[k];
+        src_total += (size_t)heights[i] * widths[i] * channels;
+        tmp_max = std::max(tmp_max, (size_t)heights[i] * tw * 3);
+      }
+      int r = G4M_OK;
+      if (ensure(d.io_src, src_total) || ensure(d.io_tmp, tmp_max * 4) || ensure(d.io_in, cnt * img * 4) ||
+          ensure(d.io_out, cnt * ob * 4))
+        r = fail(G4M_E_CUDA, "io allocation failed");
+      cudaStream_t st = d.st;
+      size_t off = 0;
+      for (int k = lo; !r && k < hi; ++k) {  // upload and resize each source to the group's target size
+        const int i = grp[k];
+        const size_t bytes = (size_t)heights[i] * widths[i] * channels;
+        if (cudaMemcpyAsync((uint8_t*)d.io_src.p + off, images[i], bytes, cudaMemcpyHostToDevice, st) ||
+            vision_resize((const uint8_t*)d.io_src.p + off, heights[i], widths[i], channels, th, tw,
+                          (float*)d.io_tmp.p, (float*)d.io_in.p + (size_t)(k - lo) * img, st))
+          r = fail(G4M_E_CUDA, "image upload / resize failed");
+        g_launches.fetch_add(2, std::memory_order_relaxed);
+        off += bytes;
+      }
+      if (!r) r = vision_forward(ctx, d, cnt, (const float*)d.io_in.p, th, tw, max_soft_tokens, layer_count,
+                                 (float*)d.io_out.p, st);
+      for (int k = lo; !r && k < hi; ++k)
+        if (cudaMemcpyAsync(out[grp[k]], (float*)d.io_out.p + (size_t)(k - lo) * ob, ob * 4, cudaMemcpyDeviceToHost, st))
+          r = fail(G4M_E_CUDA, "embedding download failed");
+      if (!r) r = finish(d, st);
+      for (int k = lo; k < hi; ++k) {
+        rcs[grp[k]] = r;
+        if (r) msgs[grp[k]] = tl_err;
+        else if (rows_out) rows_out[grp[k]] = tokens;
+      }
+    };
+    if (G == 1) work(0);
+    else {
+      std::vector<std::thread> ths;
+      for (int g = 0; g < G; ++g) ths.emplace_back(work, g);
+      for (auto& t : ths) t.join();
+    }
+  }
+  int first = G4M_OK;
+  for (int i = 0; i < n; ++i) {
+    if (status) status[i] = rcs[i];
+    if (rcs[i] && !first) {
+      first = rcs[i];
+      tl_err = msgs[i];
     }
   }
   return first;

@@ -123,6 +123,25 @@ G4M_API int g4m_vision_embed_batch(g4m_ctx* ctx, int n, const float* const* pixe
 G4M_API int g4m_vision_embed_device(g4m_ctx* ctx, int device_index, int n, const float* pixels_dev, int height, int width,
                             int max_soft_tokens, int layer_count, float* out_dev, void* stream);
 
+/* Image embeddings for n decoded 8-bit images of any size
+ * (computeGemma4VisionImageEmbeddings with preprocessGemma4ImageBlob,
+ * src/vision/index.ts:12-148, src/preprocess/image.ts:104-162, batched):
+ * images[i] is RGB or RGBA uint8 [heights[i]][widths[i]][channels].  Each
+ * image is resized on the device to its token layout's target size
+ * (antialiased linear filter, 8-bit rounding, 1/255 rescale) and embedded;
+ * images with the same target size share a batch.  out[i] receives
+ * [soft_tokens_i][1536] float32, rows_out[i] the token count, status[i]. */
+G4M_API int g4m_vision_embed_images(g4m_ctx* ctx, int n, const uint8_t* const* images, const int* heights,
+                                    const int* widths, int channels, int max_soft_tokens, int layer_count,
+                                    float* const* out, int* rows_out, int* status);
+
+/* The resize step of g4m_vision_embed_images on its own (host buffers):
+ * uint8 [height][width][channels] -> float32 [target_height][target_width][3]
+ * in [0, 1] (replaces the canvas drawImage + getImageData * rescaleFactor of
+ * src/preprocess/image.ts:121-151). */
+G4M_API int g4m_resize_rgb(g4m_ctx* ctx, int device_index, const uint8_t* src, int height, int width, int channels,
+                           int target_height, int target_width, float* dst);
+
 /* Stage outputs of the last g4m_vision_embed_device call on a device, for
  * layer-anchored parity checks: which = 0 patch embeddings [n*N][768],
  * 1 final hidden states [n*N][768].  Host copy; returns G4M_E_ARG if the

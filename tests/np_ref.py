@@ -205,3 +205,26 @@ def audio_layer(W, i, h):
     h3 = h2 + lin(f"{p}.lconv1d.linear_end.linear", x, D, D)
     h4 = ffn("feed_forward2", h3)
     return rmsnorm(h4, W[f"{p}.norm_out.weight"])
+
+
+def resize_rgb(img, th, tw):
+    """Antialiased linear (triangle) resize of uint8 [h, w, c] to float
+    [th, tw, 3] in [0, 1] with 8-bit rounding: the filter the device uses for
+    the canvas drawImage step (radius max(scale, 1), centre (i + 0.5) scale)."""
+    img = np.asarray(img, np.float64)[..., :3]
+
+    def axis(n_in, n_out):
+        s = n_in / n_out
+        r = max(s, 1.0)
+        m = np.zeros((n_out, n_in))
+        for i in range(n_out):
+            c = (i + 0.5) * s
+            x = np.arange(max(0, int(np.floor(c - r))), min(n_in - 1, int(np.ceil(c + r))) + 1)
+            w = np.maximum(0.0, 1.0 - np.abs(x + 0.5 - c) / r)
+            m[i, x] = w / w.sum()
+        return m
+
+    h, w = img.shape[:2]
+    tmp = np.einsum("ox,yxc->yoc", axis(w, tw), img)
+    out = np.einsum("oy,yxc->oxc", axis(h, th), tmp)
+    return (np.clip(np.floor(out + 0.5), 0, 255) / 255.0).astype(np.float32)
