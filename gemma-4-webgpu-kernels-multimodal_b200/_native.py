@@ -39,6 +39,7 @@ _SIGS = [
     ("g4m_linear_run_noalloc", _I, [_VP, _VP, _I, _VP, _VP]),
     ("g4m_vision_embed_images", _I, [_VP, _I, _VP, _VP, _VP, _I, _I, _I, _VP, _VP, _VP]),
     ("g4m_resize_rgb", _I, [_VP, _I, _VP, _I, _I, _I, _I, _I, _VP]),
+    ("g4m_selftest_wait_timeout", _I, [_VP, _I, ctypes.c_longlong]),
     ("g4m_vision_embed_batch", _I, [_VP, _I, _VP, _I, _I, _I, _I, _VP, _VP, _VP]),
     ("g4m_vision_embed_device", _I, [_VP, _I, _I, _VP, _I, _I, _I, _I, _VP, _VP]),
     ("g4m_vision_debug_hidden", _I, [_VP, _I, _I, _VP, ctypes.c_size_t]),

@@ -114,6 +114,8 @@ struct RowArgs {
   long lda;
 };
 cudaError_t fused_rows(const RowArgs& r, cudaStream_t st);
+// One-warp kernel whose bounded wait expires after `budget` cycles (sets *err).
+cudaError_t selftest_wait_timeout(int* err, long long budget, cudaStream_t st);
 
 // Vision helpers -- kernels_vision.cu
 cudaError_t vision_patch_operand(const float* pixels, int n_images, int height, int width, int patch, __half* hi,

@@ -52,22 +52,27 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait: returns false (and records `code` in *err) when the phase
-// does not complete within kWaitCycles, or when another warp of the CTA
+// does not complete within `budget` cycles, or when another warp of the CTA
 // already aborted (*abort_flag != 0).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
-                                          volatile int* abort_flag) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* err, int code,
+                                              volatile int* abort_flag, long long budget) {
   const uint32_t b = smem_u32(bar);
   if (mbar_try_wait(b, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_wait(b, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > budget) {
       atomicCAS(err, 0, code);
       *abort_flag = 1;
       return false;
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          volatile int* abort_flag) {
+  return mbar_wait_for(bar, parity, err, code, abort_flag, kWaitCycles);
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {

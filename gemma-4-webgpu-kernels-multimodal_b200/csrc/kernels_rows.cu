@@ -201,4 +201,26 @@ cudaError_t gather_rows(const float* src, const int* rows_idx, long n, int d, fl
   return cudaGetLastError();
 }
 
+// Self-test of the device-side failure detection: one warp waits on a shared
+// mbarrier that nothing arrives on, through the same bounded wait the GEMM
+// and attention pipelines use, so the wait expires after `budget` cycles,
+// records kErrWaitFull in the error word and the kernel returns.
+__global__ void wait_timeout_kernel(int* err, long long budget) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) (void)mbar_wait_for(&bar, 0, err, kErrWaitFull, &abort_flag, budget);
+}
+
+cudaError_t selftest_wait_timeout(int* err, long long budget, cudaStream_t st) {
+  if (budget <= 0) return cudaErrorInvalidValue;
+  wait_timeout_kernel<<<1, 32, 0, st>>>(err, budget);
+  return cudaGetLastError();
+}
+
 }  // namespace g4m

@@ -996,6 +996,18 @@ int g4m_vision_embed_images(g4m_ctx* ctx, int n, const uint8_t* const* images, c
   return first;
 }
 
+int g4m_selftest_wait_timeout(g4m_ctx* ctx, int di, long long budget_cycles) {
+  if (!ctx || di < 0 || di >= (int)ctx->devs.size() || budget_cycles <= 0 || budget_cycles > 4000000000LL)
+    return fail(G4M_E_ARG, "bad argument");
+  Device& d = *ctx->devs[di];
+  std::lock_guard<std::mutex> lk(d.mu);
+  cudaSetDevice(d.id);
+  (void)cudaGetLastError();
+  cudaStream_t st = d.st;
+  G4M_RUN("selftest_wait", selftest_wait_timeout(d.err, budget_cycles, st));
+  return finish(d, st);  // reads and clears the error word: G4M_E_TIMEOUT expected
+}
+
 int g4m_vision_debug_hidden(g4m_ctx* ctx, int di, int which, float* host, size_t count) {
   if (!ctx || di < 0 || di >= (int)ctx->devs.size() || !host) return fail(G4M_E_ARG, "bad argument");
   Device& d = *ctx->devs[di];

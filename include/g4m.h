@@ -197,6 +197,14 @@ G4M_API double g4m_checksum_floats(const float* values, int64_t count);
 
 /* ------------------------------------------------------ instrumentation */
 
+/* Self-test of the device-side failure detection (no reference counterpart):
+ * launches one warp that waits on a barrier nothing arrives on, through the
+ * kernels' bounded wait with a budget of budget_cycles (1 .. 4e9), and
+ * returns the resulting status: G4M_E_TIMEOUT with the kernel's error code in
+ * g4m_last_error().  The error word is cleared, so the context stays usable.
+ * Nothing faults or hangs. */
+G4M_API int g4m_selftest_wait_timeout(g4m_ctx* ctx, int device_index, long long budget_cycles);
+
 /* Per-launch CUDA-event timing on one device: begin, run calls, end.  The
  * end call waits for the recorded events and writes a JSON object
  * {"label": [launches, total_ms], ...} into buf. */
