@@ -101,13 +101,19 @@ int load_audio(Device& d, const SafeTensors& f) {
   aw.c0w = up(d, c0, f);
   aw.c0n = up(d, c0n, f);
   aw.c1n = up(d, c1n, f);
-  {  // layer-1 conv transposed to [kt][kf][c_in][c_out]
+  {  // layer-1 conv as tap-major rows [kt * 3 + kf][c_out][c_in], fp16 hi / lo (the conv GEMM's B operand)
     const float* w = (const float*)f.data(*c1);
-    std::vector<float> t((size_t)9 * 128 * 32);
+    std::vector<float> t((size_t)9 * 32 * 128);
     for (int co = 0; co < 32; ++co)
       for (int ci = 0; ci < 128; ++ci)
-        for (int k = 0; k < 9; ++k) t[((size_t)k * 128 + ci) * 32 + co] = w[((size_t)co * 128 + ci) * 9 + k];
-    aw.c1w = upload_f32(d, t.data(), t.size());
+        for (int k = 0; k < 9; ++k) t[((size_t)k * 32 + co) * 128 + ci] = w[((size_t)co * 128 + ci) * 9 + k];
+    aw.c1_hi = (__half*)dalloc(d, t.size() * 2);
+    aw.c1_lo = (__half*)dalloc(d, t.size() * 2);
+    if (!aw.c1_hi || !aw.c1_lo || ensure(staging, t.size() * 4) != cudaSuccess ||
+        cudaMemcpy(staging.p, t.data(), t.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        prep_w(staging.p, 2, 0, 9 * 32, 128, nullptr, aw.c1_hi, aw.c1_lo, 0) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess)
+      return fail(G4M_E_CUDA, "audio subsample weight upload failed");
   }
   aw.out_b = up(d, ob, f);
   auto split_upload = [&](const TensorInfo* t, int rows, int cols, __half** hi, __half** lo) -> int {
@@ -588,17 +594,19 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
     slen[i] = shapes[i].samples;
     FR += shapes[i].frames;
     const int t0 = (shapes[i].frames - 1) / 2 + 1;  // layer-0 rows (src/audio/kernels.ts:1242-1244)
-    t0off[i] = (int)T0S;
-    T0S += t0;
+    t0off[i] = (int)T0S + 1;                        // a zero row before every clip
+    T0S += t0 + 1;
     max_t0 = std::max(max_t0, t0);
   }
+  T0S += 1;            // and one after the last
+  T0S += T0S & 1;      // an even row count (the conv's TMA view pairs rows)
   long M = 0;
   int nblocks = 0;
   if ((rc = audio_setup_rows(d, rows, &M, &nblocks, st))) return rc;
   AudioBuffers& b = d.ab;
   if (ensure(b.sample_off, n * 8) || ensure(b.sample_len, n * 8) || ensure(b.frame_off, n * 4) ||
       ensure(b.frames, n * 4) || ensure(b.feats, FR * 128 * 4) || ensure(b.t0_off, n * 4) ||
-      ensure(b.l0, (size_t)T0S * 64 * 128 * 4))
+      ensure(b.l0, (size_t)T0S * 64 * 128 * 2 * 2))
     return fail(G4M_E_CUDA, "audio front-end allocation failed");
   G4M_LAUNCH_A(cudaMemcpyAsync(b.sample_off.p, soff.data(), n * 8, cudaMemcpyHostToDevice, st));
   G4M_LAUNCH_A(cudaMemcpyAsync(b.sample_len.p, slen.data(), n * 8, cudaMemcpyHostToDevice, st));
@@ -614,9 +622,12 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   G4M_RUN("logmel", audio_logmel(samples_dev, (const long*)b.sample_off.p, (const long*)b.sample_len.p, dfoff, dfcnt, n,
                                  (int)FR, aw.window, aw.mel, aw.mel_rng, aw.twiddle, (float*)b.feats.p, st));
   const int max_rows = *std::max_element(rows.begin(), rows.end());
-  G4M_RUN("subsample", audio_subsample((const float*)b.feats.p, dfoff, dfcnt, (const int*)b.t0_off.p,
-                                       (const int*)b.clip_row0.p, (const int*)b.clip_rows.p, n, max_t0, max_rows,
-                                       aw.c0w, aw.c0n, aw.c1w, aw.c1n, 1e-6f, (float*)b.l0.p, ah, al, st));
+  __half* l0h = (__half*)b.l0.p;
+  __half* l0l = l0h + (size_t)T0S * 64 * 128;
+  G4M_RUN("subsample", audio_subsample_tc((const float*)b.feats.p, dfoff, dfcnt, (const int*)b.t0_off.p, T0S,
+                                          (const int*)b.clip_row0.p, (const int*)b.clip_rows.p, n, max_t0, max_rows,
+                                          aw.c0w, aw.c0n, aw.c1_hi, aw.c1_lo, aw.c1n, 1e-6f, l0h, l0l, ah, al, d.err,
+                                          st));
   GemmArgs a = aargs(d, M, D, D);
   a.out_f32 = h;
   a.ldo = D;

@@ -139,12 +139,15 @@ cudaError_t vision_attention_tc(const __half* q_hi, const __half* q_lo, const __
 cudaError_t audio_logmel(const float* samples, const long* sample_off, const long* sample_len, const int* frame_off,
                          const int* frames, int clips, int total_frames, const float* window, const float* mel,
                          const int* mel_rng, const double2* twiddle, float* features, cudaStream_t st);
-// Layer-0 rows of clip i start at packed layer-0 row t0off[i] of l0 (scratch
-// [sum T0][64][128] f32); output rows at packed row row0[i], rows[i] of them.
-cudaError_t audio_subsample(const float* feats, const int* frame_off, const int* frames, const int* t0off,
-                            const int* row0, const int* rows, int clips, int max_t0, int max_rows, const float* w0,
-                            const float* n0, const float* w1t, const float* n1, float eps, float* l0, __half* a_hi,
-                            __half* a_lo, cudaStream_t st);
+// Subsample convs.  Layer-0 rows of clip i start at row t0off[i] of the fp16
+// hi / lo planes l0h, l0l ([l0_rows][64][128]; a zero row precedes and
+// follows every clip); output rows at packed row row0[i], rows[i] of them.
+// w1_hi / w1_lo: layer-1 weights [9 taps][32 out][128 in].
+cudaError_t audio_subsample_tc(const float* feats, const int* frame_off, const int* frames, const int* t0off,
+                               long l0_rows, const int* row0, const int* rows, int clips, int max_t0, int max_rows,
+                               const float* w0, const float* n0, const __half* w1_hi, const __half* w1_lo,
+                               const float* n1, float eps, __half* l0h, __half* l0l, __half* a_hi, __half* a_lo,
+                               int* err, cudaStream_t st);
 cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
                                    const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
                                    float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st);

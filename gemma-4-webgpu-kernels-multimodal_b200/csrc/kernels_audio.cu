@@ -96,209 +96,6 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 }
 
 // ---------------------------------------------------------------------------
-// Subsample convs (runAudioSubsampleConvLayerCpu twice,
-// src/audio/kernels.ts:112-183).  Source rows outside the clip are skipped,
-// as masked or out-of-range source times are in the reference.
-//
-// Layer 0 (1 -> 128 channels, 3x3 stride 2, channel LayerNorm with weight,
-// ReLU): one CTA per (layer-0 row, clip), one warp per frequency, lane =
-// channels lane + 32 j; the 128-channel statistics are warp reductions in
-// double.  Output l0 [packed layer-0 rows][64 freq][128 channels] f32.
-// w0: [128][3][3].
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restrict__ feats, const int* __restrict__ foff,
-                                                           const int* __restrict__ fcount, const int* __restrict__ t0off,
-                                                           const float* __restrict__ w0, const float* __restrict__ n0,
-                                                           float eps, float* __restrict__ l0) {
-  __shared__ float xs[3][128];
-  const int clip = blockIdx.y, t0 = blockIdx.x;
-  const int F = fcount[clip];
-  const int T0 = (F - 1) / 2 + 1;
-  if (t0 >= T0) return;
-  const float* fx = feats + (long)foff[clip] * 128;
-  for (int i = threadIdx.x; i < 3 * 128; i += 256) {
-    const int r = 2 * t0 - 1 + i / 128;
-    xs[i / 128][i % 128] = (r >= 0 && r < F) ? fx[(long)r * 128 + (i % 128)] : 0.f;
-  }
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float w[4][9], nw[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-#pragma unroll
-    for (int k = 0; k < 9; ++k) w[j][k] = __ldg(w0 + (lane + 32 * j) * 9 + k);
-    nw[j] = __ldg(n0 + lane + 32 * j);
-  }
-  float* dst = l0 + ((long)t0off[clip] + t0) * 64 * 128;
-  for (int f0 = warp; f0 < 64; f0 += 8) {
-    float v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float s = 0.f;
-#pragma unroll
-      for (int kt = 0; kt < 3; ++kt)
-#pragma unroll
-        for (int kf = 0; kf < 3; ++kf) {
-          const int sf = 2 * f0 + kf - 1;
-          if (sf >= 0 && sf < 128) s = fmaf(xs[kt][sf], w[j][kt * 3 + kf], s);
-        }
-      v[j] = s;
-    }
-    double sum = (double)v[0] + (double)v[1] + (double)v[2] + (double)v[3];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const double mean = sum / 128.0;
-    double var = 0.0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) var += ((double)v[j] - mean) * ((double)v[j] - mean);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-    const double inv = 1.0 / sqrt(var / 128.0 + (double)eps);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const double y = ((double)v[j] - mean) * inv * (double)nw[j];
-      dst[f0 * 128 + lane + 32 * j] = y > 0.0 ? (float)y : 0.f;
-    }
-  }
-}
-
-// Layer 1 (128 -> 32 channels, 3x3 stride 2, LayerNorm, ReLU) -> the
-// [32 freq x 32 channel] row (index f * 32 + c) as the fp16 hi/lo operand of
-// the input projection.  One CTA = 8 consecutive output rows t1 of one clip
-// (grid y = clip), one warp per row, lane = output frequency f1, 32 channel
-// accumulators per thread.  The 17 layer-0 rows those rows read are staged
-// 16 input channels at a time as even-frequency (f0 = 2 j) and odd-frequency
-// (f0 = 2 j - 1, j = 0 the zero padding) planes, so the three frequency taps
-// of a lane are consecutive, bank-conflict-free rows, and the chunk's
-// weights are warp-uniform broadcast loads (1 + 8 vector loads per 32 FMAs).
-// f32 accumulation (1152 terms per output).  w1t: [3][3][128 in][32 out].
-namespace sub {
-constexpr int RT = 8;                 // output rows per CTA
-constexpr int L0R = 2 * RT + 1;       // layer-0 rows read
-constexpr int CC = 16;                // input channels per chunk
-constexpr int CP = CC + 1;            // channel pitch (bank-conflict-free lanes)
-constexpr int FI = 65;                // 32 even + 33 odd frequency slots
-constexpr int L0C = L0R * FI * CP;    // floats
-constexpr int WC = 9 * CC * 32;       // floats
-constexpr int SMEM = (WC + L0C) * 4;
-}  // namespace sub
-
-__global__ void __launch_bounds__(256, 2) subsample_l1_kernel(const float* __restrict__ l0g, const int* __restrict__ t0off,
-                                                              const int* __restrict__ fcount, const int* __restrict__ row0,
-                                                              const int* __restrict__ rows, const float* __restrict__ w1t,
-                                                              const float* __restrict__ n1, float eps,
-                                                              __half* __restrict__ a_hi, __half* __restrict__ a_lo) {
-  using namespace sub;
-  extern __shared__ __align__(16) float smf[];
-  float* wc = smf;                      // [9][CC][32] layer-1 weights of the chunk
-  float* l0 = wc + WC;                  // [L0R][FI][CP] one channel chunk of layer 0
-  const int clip = blockIdx.y;
-  const int R = rows[clip];
-  const int t1_0 = blockIdx.x * RT;
-  if (t1_0 >= R) return;
-  const int T0 = (fcount[clip] - 1) / 2 + 1;
-  const float* src = l0g + (long)t0off[clip] * 64 * 128;
-  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-  const int r0 = 2 * t1_0 - 1;          // first layer-0 row
-  float acc[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-  const int t1 = t1_0 + warp;
-  for (int cc = 0; cc < 128; cc += CC) {
-    __syncthreads();  // previous chunk consumed
-    for (int i = t; i < WC / 4; i += 256) {
-      const int tap = i / (CC * 8), rem = i % (CC * 8);
-      reinterpret_cast<float4*>(wc)[i] =
-          __ldg(reinterpret_cast<const float4*>(w1t + ((long)tap * 128 + cc) * 32) + rem);
-    }
-    for (int i = t; i < L0R * FI * CC; i += 256) {
-      const int c = i % CC, slot = (i / CC) % FI, rr = i / (CC * FI);
-      const int f0 = slot < 32 ? 2 * slot : 2 * (slot - 32) - 1;
-      const int t0 = r0 + rr;
-      l0[(rr * FI + slot) * CP + c] =
-          (f0 >= 0 && t0 >= 0 && t0 < T0) ? __ldg(src + ((long)t0 * 64 + f0) * 128 + cc + c) : 0.f;
-    }
-    __syncthreads();
-    if (t1 < R) {
-#pragma unroll 1
-      for (int kt = 0; kt < 3; ++kt) {
-        const int rr = 2 * warp + kt;
-#pragma unroll
-        for (int kf = 0; kf < 3; ++kf) {
-          const int slot = kf == 1 ? lane : 32 + lane + (kf == 2 ? 1 : 0);
-          const float* a = l0 + (rr * FI + slot) * CP;
-          const float4* w4 = reinterpret_cast<const float4*>(wc + (kt * 3 + kf) * CC * 32);
-#pragma unroll 4
-          for (int c = 0; c < CC; ++c) {
-            const float av = a[c];
-#pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const float4 w = w4[c * 8 + q];
-              acc[4 * q] = fmaf(av, w.x, acc[4 * q]);
-              acc[4 * q + 1] = fmaf(av, w.y, acc[4 * q + 1]);
-              acc[4 * q + 2] = fmaf(av, w.z, acc[4 * q + 2]);
-              acc[4 * q + 3] = fmaf(av, w.w, acc[4 * q + 3]);
-            }
-          }
-        }
-      }
-    }
-  }
-  if (t1 >= R) return;
-  // LayerNorm over the 32 channels of (t1, f1 = lane) in double, then ReLU
-  double mean = 0.0;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) mean += (double)acc[j];  // channelValues is a Float32Array
-  mean /= 32.0;
-  double var = 0.0;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const double dv = (double)acc[j] - mean;
-    var += dv * dv;
-  }
-  const double inv = 1.0 / sqrt(var / 32.0 + (double)eps);
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const double nv = ((double)acc[j] - mean) * inv * (double)__ldg(n1 + j);
-    v[j] = nv > 0.0 ? (float)nv : 0.f;
-  }
-  const long orow = (long)row0[clip] + t1;
-  __half* dh = a_hi + orow * 1024 + lane * 32;
-  __half* dl = a_lo + orow * 1024 + lane * 32;
-#pragma unroll
-  for (int j = 0; j < 32; j += 8) {
-    uint32_t hv[4], lv[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) split2_f16(v[j + 2 * u], v[j + 2 * u + 1], hv[u], lv[u]);
-    *reinterpret_cast<uint4*>(dh + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-    *reinterpret_cast<uint4*>(dl + j) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-  }
-}
-
-cudaError_t audio_subsample(const float* feats, const int* frame_off, const int* frames, const int* t0off,
-                            const int* row0, const int* rows, int clips, int max_t0, int max_rows, const float* w0,
-                            const float* n0, const float* w1t, const float* n1, float eps, float* l0, __half* a_hi,
-                            __half* a_lo, cudaStream_t st) {
-  if (clips <= 0 || max_rows <= 0) return cudaSuccess;
-  if (clips > 65535) return cudaErrorInvalidValue;  // grid y = clip
-  static bool attr[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(subsample_l1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sub::SMEM);
-    if (e != cudaSuccess) return e;
-    attr[dev] = true;
-  }
-  subsample_l0_kernel<<<dim3(max_t0, clips), 256, 0, st>>>(feats, frame_off, frames, t0off, w0, n0, eps, l0);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  dim3 grid((max_rows + sub::RT - 1) / sub::RT, clips);
-  subsample_l1_kernel<<<grid, 256, sub::SMEM, st>>>(l0, t0off, frames, row0, rows, w1t, n1, eps, a_hi, a_lo);
-  return cudaGetLastError();
-}
-
-// ---------------------------------------------------------------------------
 // Chunked local self-attention (runAudioSelfAttentionBodyCpu and
 // audioSelfAttentionScore, src/audio/kernels.ts:432-512): chunk 12, context
 // 24 (12 past-horizon rows), 13 relative positions, per-dim softplus query

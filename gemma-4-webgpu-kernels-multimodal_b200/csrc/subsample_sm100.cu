@@ -1,0 +1,326 @@
+// Audio subsample convs on sm_100a (runAudioSubsampleConvLayerCpu twice,
+// src/audio/kernels.ts:112-183, and the flatten of runAudioSubsampleProjectionCpu,
+// 22-62).  Source rows outside the clip are skipped, as masked or out-of-range
+// source times are in the reference.
+//
+// Layer 0 (1 -> 128 channels, 3x3 stride 2, channel LayerNorm with weight,
+// ReLU): one CTA per (layer-0 row, clip), one warp per frequency, lane =
+// channels lane + 32 j; statistics are warp reductions in double.  The result
+// is stored as fp16 hi / lo planes [rows][64 freq][128 ch] in which every
+// clip's rows are preceded and followed by a zero row, so a layer-1 tap that
+// leaves the clip reads zeros.
+//
+// Layer 1 (128 -> 32 channels, 3x3 stride 2, LayerNorm, ReLU) is an implicit
+// GEMM on tcgen05: M = 128 output positions (4 rows x 32 frequencies), N = 32
+// channels, K = 9 taps x 128 channels.  The layer-0 planes are described to
+// TMA as 5-D tensors (channel, frequency parity, frequency / 2, row parity,
+// row / 2), so for each tap (kt, kf) and 64-channel half the stride-2 im2col
+// tile L0[2 t1 + kt - 1][2 f1 + kf - 1][c] is one dense box (64 channels x 32
+// frequencies x 4 rows at fixed parities) landing in the 128-byte swizzled
+// K-major layout the MMA reads (frequency -1 is an out-of-range, zero-filled
+// coordinate).  Operands are fp16 hi / lo planes, three terms
+// (Ah Bh + Ah Bl + Al Bh) accumulate in f32 in TMEM.  The epilogue thread of
+// position (t1, f1) holds its 32 channels, so the LayerNorm is thread-local
+// (double statistics, as the reference's JS numbers).
+//   warp 0  TMA producer (3-stage ring)   warp 1  TMEM owner + MMA issuer
+//   warps 2..5  epilogue (warp % 4 = output row of the tile, lane = f1)
+#include "g4m_kernels.h"
+#include "g4m_sm100.cuh"
+
+namespace g4m {
+
+namespace {
+constexpr int SA_BYTES = 128 * 128;  // A tile: 128 positions x 64 channels fp16
+constexpr int SB_BYTES = 32 * 128;   // B tile: 32 output channels x 64 channels fp16
+constexpr int SSTAGE = 2 * SA_BYTES + 2 * SB_BYTES;
+constexpr int SSTAGES = 3;
+constexpr int SKB = 18;              // k-blocks: 9 taps x 2 channel halves
+constexpr int SUB_SMEM = SSTAGES * SSTAGE + 1024;
+constexpr int SUB_THREADS = 192;
+constexpr int L0_ROW = 64 * 128;     // elements of one layer-0 row
+
+__device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+
+__device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity, int* err) {
+  const uint32_t b = smem_u32(bar);
+  const long long t0 = clock64();
+  while (!mbar_try_wait(b, parity)) {
+    if (clock64() - t0 > kWaitCycles) {
+      atomicCAS(err, 0, kErrWaitDrain);
+      return;
+    }
+  }
+}
+}  // namespace
+
+__global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restrict__ feats, const int* __restrict__ foff,
+                                                           const int* __restrict__ fcount, const int* __restrict__ t0off,
+                                                           const float* __restrict__ w0, const float* __restrict__ n0,
+                                                           float eps, __half* __restrict__ l0h,
+                                                           __half* __restrict__ l0l) {
+  __shared__ float xs[3][128];
+  const int clip = blockIdx.y, t0 = blockIdx.x;
+  const int F = fcount[clip];
+  const int T0 = (F - 1) / 2 + 1;
+  if (t0 > T0) return;
+  if (t0 == T0) {  // the zero row after the clip (and, for clip 0, the one before it)
+    const long r = (long)t0off[clip] + T0;
+    for (int i = threadIdx.x; i < L0_ROW; i += 256) {
+      l0h[r * L0_ROW + i] = __float2half_rn(0.f);
+      l0l[r * L0_ROW + i] = __float2half_rn(0.f);
+      if (clip == 0) {
+        l0h[(long)(t0off[0] - 1) * L0_ROW + i] = __float2half_rn(0.f);
+        l0l[(long)(t0off[0] - 1) * L0_ROW + i] = __float2half_rn(0.f);
+      }
+    }
+    return;
+  }
+  const float* fx = feats + (long)foff[clip] * 128;
+  for (int i = threadIdx.x; i < 3 * 128; i += 256) {
+    const int r = 2 * t0 - 1 + i / 128;
+    xs[i / 128][i % 128] = (r >= 0 && r < F) ? fx[(long)r * 128 + (i % 128)] : 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float w[4][9], nw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+#pragma unroll
+    for (int k = 0; k < 9; ++k) w[j][k] = __ldg(w0 + (lane + 32 * j) * 9 + k);
+    nw[j] = __ldg(n0 + lane + 32 * j);
+  }
+  const long row = (long)t0off[clip] + t0;
+  for (int f0 = warp; f0 < 64; f0 += 8) {
+    float v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float s = 0.f;
+#pragma unroll
+      for (int kt = 0; kt < 3; ++kt)
+#pragma unroll
+        for (int kf = 0; kf < 3; ++kf) {
+          const int sf = 2 * f0 + kf - 1;
+          if (sf >= 0 && sf < 128) s = fmaf(xs[kt][sf], w[j][kt * 3 + kf], s);
+        }
+      v[j] = s;
+    }
+    double sum = (double)v[0] + (double)v[1] + (double)v[2] + (double)v[3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    const double mean = sum / 128.0;
+    double var = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) var += ((double)v[j] - mean) * ((double)v[j] - mean);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
+    const double inv = 1.0 / sqrt(var / 128.0 + (double)eps);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const double y = ((double)v[j] - mean) * inv * (double)nw[j];
+      __half h, l;
+      split_f16(y > 0.0 ? (float)y : 0.f, h, l);
+      l0h[row * L0_ROW + f0 * 128 + lane + 32 * j] = h;
+      l0l[row * L0_ROW + f0 * 128 + lane + 32 * j] = l;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(SUB_THREADS, 1)
+    subsample_conv_tc_kernel(const __grid_constant__ CUtensorMap mLh, const __grid_constant__ CUtensorMap mLl,
+                             const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
+                             const int* __restrict__ t0off, const int* __restrict__ row0, const int* __restrict__ rows,
+                             const float* __restrict__ n1, float eps, __half* __restrict__ a_hi,
+                             __half* __restrict__ a_lo, int* err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bar_full[SSTAGES], bar_empty[SSTAGES], bar_acc;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag, skip;
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int clip = blockIdx.y;
+  const int R = rows[clip];
+  const int t1_0 = blockIdx.x * 4;
+  if (t1_0 >= R) return;  // whole CTA: nothing of this clip here
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    skip = *reinterpret_cast<volatile int*>(err) != 0;
+    abort_flag = 0;
+    for (int s = 0; s < SSTAGES; ++s) {
+      mbar_init(&bar_full[s], 1);
+      mbar_init(&bar_empty[s], 1);
+    }
+    mbar_init(&bar_acc, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (skip) return;  // an earlier kernel on this device already failed
+  if (warp == 1) tmem_alloc(&tmem_slot, 32);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  auto sA = [&](int s, int plane) { return sm + s * SSTAGE + plane * SA_BYTES; };
+  auto sB = [&](int s, int plane) { return sm + s * SSTAGE + 2 * SA_BYTES + plane * SB_BYTES; };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&mLh);
+      prefetch_tmap(&mWh);
+      const int zbase = t0off[clip] + 2 * t1_0 - 1;  // layer-0 row of tap kt = 0 for the tile's first output row
+      int issued = 0;
+      for (int kb = 0; kb < SKB; ++kb) {
+        const int s = kb % SSTAGES, tap = kb >> 1, half = kb & 1, kt = tap / 3, kf = tap % 3;
+        // frequency 2 f1 + kf - 1: parity 0 for kf = 1, else 1; half index f1 - 1 (kf = 0) or f1
+        const int fpar = kf == 1 ? 0 : 1, fh = kf == 0 ? -1 : 0;
+        const int rr = zbase + kt;  // >= 0: a zero row precedes every clip
+        if (!mbar_wait(&bar_empty[s], ((kb / SSTAGES) & 1) ^ 1, err, kErrWaitEmpty, &abort_flag)) break;
+        mbar_expect_tx(&bar_full[s], SSTAGE);
+        tma_load_5d(sA(s, 0), &mLh, &bar_full[s], 64 * half, fpar, fh, rr & 1, rr >> 1);
+        tma_load_5d(sA(s, 1), &mLl, &bar_full[s], 64 * half, fpar, fh, rr & 1, rr >> 1);
+        tma_load_2d(sB(s, 0), &mWh, &bar_full[s], 64 * half, 32 * tap);
+        tma_load_2d(sB(s, 1), &mWl, &bar_full[s], 64 * half, 32 * tap);
+        ++issued;
+      }
+      for (int j = issued > SSTAGES ? issued - SSTAGES : 0; j < issued; ++j)
+        drain_wait_s(&bar_full[j % SSTAGES], (j / SSTAGES) & 1, err);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(128, 32);
+      for (int kb = 0; kb < SKB; ++kb) {
+        const int s = kb % SSTAGES;
+        if (!mbar_wait(&bar_full[s], (kb / SSTAGES) & 1, err, kErrWaitFull, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t ah = smem_u32(sA(s, 0)), al = smem_u32(sA(s, 1));
+        const uint32_t bh = smem_u32(sB(s, 0)), bl = smem_u32(sB(s, 1));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint64_t dah = desc_k_sw128(ah + k * 32), dbh = desc_k_sw128(bh + k * 32);
+          mma_f16_ss(tmem, dah, dbh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_f16_ss(tmem, dah, desc_k_sw128(bl + k * 32), idesc, 1u);
+          mma_f16_ss(tmem, desc_k_sw128(al + k * 32), dbh, idesc, 1u);
+        }
+        mma_commit(&bar_empty[s]);
+      }
+      mma_commit(&bar_acc);  // every MMA above has completed when this arrives
+      drain_wait_s(&bar_acc, 0, err);
+    }
+  } else {
+    const int q = warp & 3;  // TMEM lanes 32 q .. 32 q + 31 = positions of output row t1_0 + q
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, err, kErrWaitAccFull, &abort_flag));
+    if (ok) {
+      tc_fence_after();
+      float acc[32];
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16), acc);
+      const int t1 = t1_0 + q;
+      if (t1 < R) {
+        double mean = 0.0;  // channelValues is a Float32Array: statistics in double
+#pragma unroll
+        for (int j = 0; j < 32; ++j) mean += (double)acc[j];
+        mean /= 32.0;
+        double var = 0.0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const double dv = (double)acc[j] - mean;
+          var += dv * dv;
+        }
+        const double inv = 1.0 / sqrt(var / 32.0 + (double)eps);
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const double nv = ((double)acc[j] - mean) * inv * (double)__ldg(n1 + j);
+          v[j] = nv > 0.0 ? (float)nv : 0.f;
+        }
+        const long orow = (long)row0[clip] + t1;
+        __half* dh = a_hi + orow * 1024 + lane * 32;
+        __half* dl = a_lo + orow * 1024 + lane * 32;
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint32_t hv[4], lv[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) split2_f16(v[j + 2 * u], v[j + 2 * u + 1], hv[u], lv[u]);
+          *reinterpret_cast<uint4*>(dh + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+          *reinterpret_cast<uint4*>(dl + j) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFnS)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFnS encode_fn_s() {
+  static EncodeTiledFnS fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFnS>(p);
+  }
+  return fn;
+}
+
+// Layer-0 plane [rows][64][128] fp16 (rows even) as a 5-D map (channel,
+// frequency parity, frequency / 2, row parity, row / 2): dense boxes of
+// 64 channels x 1 x 32 x 1 x 4 = one tap's 128-position im2col tile (16 KB),
+// 128-byte swizzle.
+static bool make_l0_map(CUtensorMap* map, const __half* base, long total_rows) {
+  EncodeTiledFnS fn = encode_fn_s();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) % 16) != 0 || (total_rows % 2) != 0) return false;
+  cuuint64_t dims[5] = {128, 2, 32, 2, (cuuint64_t)(total_rows / 2)};
+  cuuint64_t strides[4] = {128 * 2, 2 * 128 * 2, 64 * 128 * 2, 2 * 64 * 128 * 2};
+  cuuint32_t box[5] = {64, 1, 32, 1, 4};
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<__half*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t audio_subsample_tc(const float* feats, const int* frame_off, const int* frames, const int* t0off,
+                               long l0_rows, const int* row0, const int* rows, int clips, int max_t0, int max_rows,
+                               const float* w0, const float* n0, const __half* w1_hi, const __half* w1_lo,
+                               const float* n1, float eps, __half* l0h, __half* l0l, __half* a_hi, __half* a_lo,
+                               int* err, cudaStream_t st) {
+  if (clips <= 0 || max_rows <= 0) return cudaSuccess;
+  if (clips > 65535) return cudaErrorInvalidValue;  // grid y = clip
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(subsample_conv_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SUB_SMEM);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  subsample_l0_kernel<<<dim3(max_t0 + 1, clips), 256, 0, st>>>(feats, frame_off, frames, t0off, w0, n0, eps, l0h, l0l);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  CUtensorMap mLh, mLl, mWh, mWl;
+  if (!make_l0_map(&mLh, l0h, l0_rows) || !make_l0_map(&mLl, l0l, l0_rows) ||
+      !make_tmap_f16(&mWh, w1_hi, 9 * 32, 128, 32) || !make_tmap_f16(&mWl, w1_lo, 9 * 32, 128, 32))
+    return cudaErrorInvalidValue;
+  dim3 grid((max_rows + 3) / 4, clips);
+  subsample_conv_tc_kernel<<<grid, SUB_THREADS, SUB_SMEM, st>>>(mLh, mLl, mWh, mWl, t0off, row0, rows, n1, eps, a_hi,
+                                                                a_lo, err);
+  return cudaGetLastError();
+}
+
+}  // namespace g4m
