@@ -387,7 +387,8 @@ static void next_scales(RowArgs& r, const float* s, int n, __half* a_c) {
 
 // Row metadata of a packed batch: clip of every row, first row and row count
 // of every clip, attention blocks (clip, block of 12 rows).
-static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out, int* nblocks, cudaStream_t st) {
+static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out, int* nblocks, cudaStream_t st,
+                            HostKeep* keep = nullptr) {
   const int n = (int)rows.size();
   std::vector<int> row0(n);
   std::vector<int> bclip, bidx;
@@ -414,12 +415,12 @@ static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out
   for (int i = 0; i < d.aw.layers; ++i) codes3 = codes3 || d.aw.L[i].sin_qkv[0] != 0.0f;
   if (codes3 && ensure(b.a_c, M * D * 2))
     return fail(G4M_E_CUDA, "audio activation allocation failed (" + std::to_string(M) + " rows)");
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.clip_row0.p, row0.data(), n * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.clip_rows.p, rows.data(), n * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.row_clip.p, row_clip.data(), M * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.t1_off.p, bclip.data(), bclip.size() * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.t1_len.p, bidx.data(), bidx.size() * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaStreamSynchronize(st));  // the host vectors above are the copy sources
+  G4M_LAUNCH_A(upload_meta(b.clip_row0.p, row0.data(), n * 4, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.clip_rows.p, rows.data(), n * 4, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.row_clip.p, row_clip.data(), M * 4, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.t1_off.p, bclip.data(), bclip.size() * 4, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.t1_len.p, bidx.data(), bidx.size() * 4, st, keep));
+  if (!keep) G4M_LAUNCH_A(cudaStreamSynchronize(st));  // the host vectors above are the copy sources
   *M_out = M;
   *nblocks = (int)bclip.size();
   return G4M_OK;
@@ -568,7 +569,8 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
 // Packed forward for clips whose samples sit in samples_dev at offsets
 // soff.  shapes[i].t1 rows per clip.
 int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes, const float* samples_dev,
-                  const std::vector<long>& soff, int sr, int layers, float* out_dev, cudaStream_t st) {
+                  const std::vector<long>& soff, int sr, int layers, float* out_dev, cudaStream_t st,
+                  HostKeep* keep = nullptr) {
   (void)cudaGetLastError();  // a failed earlier call must not leak into this one
   AudioWeights& aw = d.aw;
   if (aw.layers == 0) return fail(G4M_E_NOT_LOADED, "audio tower weights are not loaded");
@@ -602,18 +604,18 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   T0S += T0S & 1;      // an even row count (the conv's TMA view pairs rows)
   long M = 0;
   int nblocks = 0;
-  if ((rc = audio_setup_rows(d, rows, &M, &nblocks, st))) return rc;
+  if ((rc = audio_setup_rows(d, rows, &M, &nblocks, st, keep))) return rc;
   AudioBuffers& b = d.ab;
   if (ensure(b.sample_off, n * 8) || ensure(b.sample_len, n * 8) || ensure(b.frame_off, n * 4) ||
       ensure(b.frames, n * 4) || ensure(b.feats, FR * 128 * 4) || ensure(b.t0_off, n * 4) ||
       ensure(b.l0, (size_t)T0S * 64 * 128 * 2 * 2))
     return fail(G4M_E_CUDA, "audio front-end allocation failed");
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.sample_off.p, soff.data(), n * 8, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.sample_len.p, slen.data(), n * 8, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.frame_off.p, foff.data(), n * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.frames.p, fcnt.data(), n * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaMemcpyAsync(b.t0_off.p, t0off.data(), n * 4, cudaMemcpyHostToDevice, st));
-  G4M_LAUNCH_A(cudaStreamSynchronize(st));
+  G4M_LAUNCH_A(upload_meta(b.sample_off.p, soff.data(), n * 8, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.sample_len.p, slen.data(), n * 8, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.frame_off.p, foff.data(), n * 4, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.frames.p, fcnt.data(), n * 4, st, keep));
+  G4M_LAUNCH_A(upload_meta(b.t0_off.p, t0off.data(), n * 4, st, keep));
+  if (!keep) G4M_LAUNCH_A(cudaStreamSynchronize(st));
   const int* dfoff = (const int*)b.frame_off.p;
   const int* dfcnt = (const int*)b.frames.p;
   __half *ah = (__half*)b.a_hi.p, *al = (__half*)b.a_lo.p;
@@ -776,19 +778,51 @@ int g4m_audio_embed_batch(g4m_ctx* ctx, int n, const float* const* samples, cons
     int r = G4M_OK;
     if (ensure(d.ab.samples, std::max<long>(total, 1) * 4) || ensure(d.io_out, std::max<long>(rows, 1) * 1536 * 4))
       r = fail(G4M_E_CUDA, "audio io allocation failed");
-    for (size_t k = 0; !r && k < part[g].size(); ++k)
-      if (cudaMemcpyAsync((float*)d.ab.samples.p + soff[k], samples[part[g][k]], sh[k].samples * 4,
-                          cudaMemcpyHostToDevice, d.st))
-        r = fail(G4M_E_CUDA, "sample upload failed");
-    if (!r) r = audio_forward(ctx, d, sh, (const float*)d.ab.samples.p, soff, sampling_rate, layer_count, (float*)d.io_out.p, d.st);
-    long ro = 0;
-    for (size_t k = 0; !r && k < part[g].size(); ++k) {
-      if (cudaMemcpyAsync(out[part[g][k]], (float*)d.io_out.p + ro * 1536, (size_t)sh[k].t1 * 1536 * 4,
-                          cudaMemcpyDeviceToHost, d.st))
-        r = fail(G4M_E_CUDA, "embedding download failed");
-      ro += sh[k].t1;
+    // chunks of ~32 clips (longest first, so the first chunk sizes the
+    // buffers): uploads queue on the copy stream, each chunk's forward waits
+    // for its upload, each download for its forward
+    const int m = (int)part[g].size();
+    const auto chunks = batch_chunks(m, 32);
+    std::vector<cudaEvent_t> up(chunks.size()), done(chunks.size());
+    for (size_t c = 0; c < chunks.size(); ++c) {
+      cudaEventCreateWithFlags(&up[c], cudaEventDisableTiming);
+      cudaEventCreateWithFlags(&done[c], cudaEventDisableTiming);
     }
-    if (!r) r = finish(d, d.st);
+    for (size_t c = 0; !r && c < chunks.size(); ++c) {
+      for (int k = chunks[c].first; !r && k < chunks[c].second; ++k)
+        if (cudaMemcpyAsync((float*)d.ab.samples.p + soff[k], samples[part[g][k]], sh[k].samples * 4,
+                            cudaMemcpyHostToDevice, d.cst))
+          r = fail(G4M_E_CUDA, "sample upload failed");
+      if (!r && cudaEventRecord(up[c], d.cst)) r = fail(G4M_E_CUDA, "event record failed");
+    }
+    HostKeep keep;  // chunk metadata stays alive until the final synchronize
+    long ro = 0;
+    for (size_t c = 0; !r && c < chunks.size(); ++c) {
+      const int k0 = chunks[c].first, k1 = chunks[c].second;
+      std::vector<ClipShape> csh(sh.begin() + k0, sh.begin() + k1);
+      std::vector<long> coff;
+      for (int k = k0; k < k1; ++k) coff.push_back(soff[k] - soff[k0]);
+      if (cudaStreamWaitEvent(d.st, up[c], 0)) r = fail(G4M_E_CUDA, "stream wait failed");
+      if (!r)
+        r = audio_forward(ctx, d, csh, (const float*)d.ab.samples.p + soff[k0], coff, sampling_rate, layer_count,
+                          (float*)d.io_out.p + ro * 1536, d.st, &keep);
+      if (!r && (cudaEventRecord(done[c], d.st) || cudaStreamWaitEvent(d.cst, done[c], 0)))
+        r = fail(G4M_E_CUDA, "event record failed");
+      for (int k = k0; !r && k < k1; ++k) {
+        if (cudaMemcpyAsync(out[part[g][k]], (float*)d.io_out.p + ro * 1536, (size_t)sh[k].t1 * 1536 * 4,
+                            cudaMemcpyDeviceToHost, d.cst))
+          r = fail(G4M_E_CUDA, "embedding download failed");
+        ro += sh[k].t1;
+      }
+    }
+    const int rs = finish(d, d.st);
+    const cudaError_t ce = cudaStreamSynchronize(d.cst);
+    for (size_t c = 0; c < chunks.size(); ++c) {
+      cudaEventDestroy(up[c]);
+      cudaEventDestroy(done[c]);
+    }
+    if (!r) r = rs;
+    if (!r && ce != cudaSuccess) r = fail(G4M_E_CUDA, std::string("copy stream: ") + cudaGetErrorString(ce));
     rcs[g] = r;
     if (r) msgs[g] = tl_err;
   };

@@ -669,6 +669,7 @@ g4m_ctx* g4m_create(const int* devices, int n_devices) {
     d->id = id;
     cudaSetDevice(id);
     if (cudaStreamCreateWithFlags(&d->st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaStreamCreateWithFlags(&d->cst, cudaStreamNonBlocking) != cudaSuccess ||
         cudaMalloc(&d->err, sizeof(int)) != cudaSuccess || cudaMemset(d->err, 0, sizeof(int)) != cudaSuccess) {
       fail(G4M_E_CUDA, "device setup failed on device " + std::to_string(id));
       delete d;
@@ -854,16 +855,40 @@ int g4m_vision_embed_batch(g4m_ctx* ctx, int n, const float* const* pixels, int 
     const size_t img = (size_t)height * width * 3, ob = (size_t)tokens * 1536;
     int r = G4M_OK;
     if (ensure(d.io_in, cnt * img * 4) || ensure(d.io_out, cnt * ob * 4)) r = fail(G4M_E_CUDA, "io allocation failed");
-    for (int i = 0; !r && i < cnt; ++i)
-      if (cudaMemcpyAsync((float*)d.io_in.p + i * img, pixels[lo + i], img * 4, cudaMemcpyHostToDevice, d.st))
-        r = fail(G4M_E_CUDA, "pixel upload failed");
-    if (!r)
-      r = vision_forward(ctx, d, cnt, (const float*)d.io_in.p, height, width, max_soft_tokens, layer_count,
-                         (float*)d.io_out.p, d.st);
-    for (int i = 0; !r && i < cnt; ++i)
-      if (cudaMemcpyAsync(out[lo + i], (float*)d.io_out.p + i * ob, ob * 4, cudaMemcpyDeviceToHost, d.st))
-        r = fail(G4M_E_CUDA, "embedding download failed");
-    if (!r) r = finish(d, d.st);
+    // chunks of ~16 images: uploads queue on the copy stream, each chunk's
+    // forward waits for its upload, each download for its forward
+    const auto chunks = batch_chunks(cnt, 16);
+    std::vector<cudaEvent_t> up(chunks.size()), done(chunks.size());
+    for (size_t k = 0; k < chunks.size(); ++k) {
+      cudaEventCreateWithFlags(&up[k], cudaEventDisableTiming);
+      cudaEventCreateWithFlags(&done[k], cudaEventDisableTiming);
+    }
+    for (size_t k = 0; !r && k < chunks.size(); ++k) {
+      for (int i = chunks[k].first; !r && i < chunks[k].second; ++i)
+        if (cudaMemcpyAsync((float*)d.io_in.p + i * img, pixels[lo + i], img * 4, cudaMemcpyHostToDevice, d.cst))
+          r = fail(G4M_E_CUDA, "pixel upload failed");
+      if (!r && cudaEventRecord(up[k], d.cst)) r = fail(G4M_E_CUDA, "event record failed");
+    }
+    for (size_t k = 0; !r && k < chunks.size(); ++k) {
+      const int c0 = chunks[k].first, cn = chunks[k].second - c0;
+      if (cudaStreamWaitEvent(d.st, up[k], 0)) r = fail(G4M_E_CUDA, "stream wait failed");
+      if (!r)
+        r = vision_forward(ctx, d, cn, (const float*)d.io_in.p + c0 * img, height, width, max_soft_tokens,
+                           layer_count, (float*)d.io_out.p + c0 * ob, d.st);
+      if (!r && (cudaEventRecord(done[k], d.st) || cudaStreamWaitEvent(d.cst, done[k], 0)))
+        r = fail(G4M_E_CUDA, "event record failed");
+      for (int i = c0; !r && i < c0 + cn; ++i)
+        if (cudaMemcpyAsync(out[lo + i], (float*)d.io_out.p + i * ob, ob * 4, cudaMemcpyDeviceToHost, d.cst))
+          r = fail(G4M_E_CUDA, "embedding download failed");
+    }
+    const int rs = finish(d, d.st);
+    const cudaError_t ce = cudaStreamSynchronize(d.cst);
+    for (size_t k = 0; k < chunks.size(); ++k) {
+      cudaEventDestroy(up[k]);
+      cudaEventDestroy(done[k]);
+    }
+    if (!r) r = rs;
+    if (!r && ce != cudaSuccess) r = fail(G4M_E_CUDA, std::string("copy stream: ") + cudaGetErrorString(ce));
     rcs[g] = r;
     if (r) msgs[g] = tl_err;
   };

@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -130,7 +131,8 @@ struct Device {
   std::vector<ProfRec> prof;
   std::vector<cudaEvent_t> ev_pool;
   size_t ev_used = 0;
-  cudaStream_t st = nullptr;
+  cudaStream_t st = nullptr;   // compute
+  cudaStream_t cst = nullptr;  // host <-> device copies of the batch calls (overlap the compute of other chunks)
   int* err = nullptr;
   VisionWeights vw;
   AudioWeights aw;
@@ -170,11 +172,34 @@ struct Device {
     if (err) cudaFree(err);
     err = nullptr;
     if (st) cudaStreamDestroy(st);
+    if (cst) cudaStreamDestroy(cst);
+    cst = nullptr;
     st = nullptr;
   }
 };
 
 int finish(Device& d, cudaStream_t st);
+
+// Small host -> device metadata uploads on a stream.  With `keep` the source
+// is copied into storage that lives until the caller's final synchronize, so
+// the host need not wait for the copy; without it the caller synchronizes.
+struct HostKeep {
+  std::vector<std::vector<char>> bufs;
+};
+inline cudaError_t upload_meta(void* dst, const void* src, size_t bytes, cudaStream_t st, HostKeep* keep) {
+  if (!keep) return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, st);
+  keep->bufs.emplace_back((const char*)src, (const char*)src + bytes);
+  return cudaMemcpyAsync(dst, keep->bufs.back().data(), bytes, cudaMemcpyHostToDevice, st);
+}
+
+// Chunks of a batch call: [begin, end) ranges of `n` items, about `per` each,
+// so the copies of one chunk overlap the compute of another.
+inline std::vector<std::pair<int, int>> batch_chunks(int n, int per) {
+  std::vector<std::pair<int, int>> c;
+  const int k = std::max(1, (n + std::max(per, 1) - 1) / std::max(per, 1));
+  for (int i = 0; i < k; ++i) c.push_back({(int)((long)n * i / k), (int)((long)n * (i + 1) / k)});
+  return c;
+}
 
 inline void prof_begin(Device& d, cudaStream_t st, const char* label) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
