@@ -191,3 +191,23 @@ def test_audio_12_layers_propagated(aud12, oracle, syn):
           f"oracle vs 1e-6-perturbed oracle cos {cos_env:.5f} max-abs/RMS {ma_env:.3e}")
     assert np.isfinite(outs[0]).all()
     assert (1 - cos) <= 3 * (1 - cos_env) + 1e-3, (cos, cos_env)
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_audio_packed_low_bit_tower(native, syn, oracle, tmp_path, bits):
+    """Audio tower checkpoints with 2- and 4-bit packed QAT weights
+    (derivePackedQatBits, src/kernels/qat.ts:199-213): one layer, 1 s clip."""
+    W = syn.audio_weights(5, layers=1, bits=bits)
+    path = str(tmp_path / f"a{bits}.safetensors")
+    syn.write_safetensors(path, W)
+    c = native.Context()
+    try:
+        c.load_weights(path)
+        x = syn.audio_samples(6, 16000)
+        hid = []
+        oracle.audio_embed(W, x, layer_count=1, hidden_out=hid)
+        c.audio_embed([x], 16000, 1)
+        got = c.audio_debug_hidden(hid[-1].shape[0])
+        assert_parity(hid[-1], got, what=f"audio layer with {bits}-bit packed weights")
+    finally:
+        c.close()
