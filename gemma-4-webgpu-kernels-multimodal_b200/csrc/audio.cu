@@ -540,7 +540,8 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
     op = GemmOperands{ah, al, L.wstart, nullptr};
     G4M_RUN("gemm_lconv_start", gemm_launch(256, L.sin_start != 0.0f ? 1 : 2, EPI_GLU, op, a, st));
     G4M_RUN("lconv",
-            audio_lconv_rows((const float*)b.g.p, L.dw, L.n_conv, drc, drow0, M, 1e-6f, ah, al, L.sin_end, st));
+            audio_lconv_rows((const float*)b.g.p, L.dw, L.n_conv, drc, drow0, M, 1e-6f, ah, al, L.sin_end,
+                             d.err, st));
     a = aargs(d, M, D, D);
     a.col_scale = L.send;
     a.s_out = L.sout_end;

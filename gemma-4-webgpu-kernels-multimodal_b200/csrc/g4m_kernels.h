@@ -152,7 +152,8 @@ cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const fl
                                    const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
                                    float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st);
 cudaError_t audio_lconv_rows(const float* g, const float* dw, const float* nw, const int* row_clip, const int* row0,
-                             long rows, float eps, __half* a_hi, __half* a_lo, float s_code, cudaStream_t st);
+                             long rows, float eps, __half* a_hi, __half* a_lo, float s_code, int* err,
+                             cudaStream_t st);
 cudaError_t gather_rows(const float* src, const int* rows_idx, long n, int d, float* dst, cudaStream_t st);
 cudaError_t row_inv_rms_operand(const float* x, long rows, int d, float eps, __half* hi, __half* lo, cudaStream_t st);
 cudaError_t add_bias_rows(float* y, const float* b, long rows, int d, cudaStream_t st);

@@ -53,23 +53,6 @@ __device__ __forceinline__ float srq_f(float v, float s) {
   return srq_code(v, s, 1.0f / s) * s;
 }
 
-__device__ __forceinline__ float ex2_approx(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-__device__ __forceinline__ float rcp_approx(float x) {
-  float y;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
-
-constexpr float kLog2eF = 1.4426950408889634f;
-
-// sigmoid(x) = 1 / (1 + 2^(-x log2 e)); saturates to 0 / 1 without NaN.
-__device__ __forceinline__ float sigmoid_f(float x) { return rcp_approx(1.0f + ex2_approx(-x * kLog2eF)); }
-
 // geluPytorchTanh (src/vision/kernels.ts:155-159):
 // 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi) (x + 0.044715 x^3).
 __device__ __forceinline__ float gelu_tanh_f(float x) {

@@ -104,8 +104,13 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 // One CTA per (clip block of 12 rows, head), 128 threads:
 //   stage    the 24-row key / value window (keys pre-scaled), the 13
 //            relative keys and the block's 12 scaled queries in shared memory
-//   dots     the 12 x 24 query-key and 12 x 13 query-relative dot products,
-//            each a float4 sequence over the 128 dims, spread over all threads
+//   dots     the 12 x 40 products of the queries with [24 keys | 13 relative
+//            keys | 3 zero rows] as a register-blocked tile product: warp w
+//            takes dims [32w, 32w + 32), lane (qg, cg) = (lane & 3, lane >> 2)
+//            a 3 x 5 block of rows 3qg.. and slots 5cg..; each float4 step
+//            loads 8 vectors (broadcast, bank-conflict free with the 132-float
+//            row pitch) for 60 FMAs; the 4 warps' partial sums meet in the
+//            softmax
 //   softmax  one warp per query row, lane = context slot: tanh softcap, max,
 //            exp, sum; weights of out-of-clip slots kept in the denominator
 //   P*V      thread = output dim, 24-term sums for each of the 12 rows
@@ -118,10 +123,15 @@ __global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict
                                                          const int* __restrict__ row0, const int* __restrict__ rows,
                                                          float kscale, float softcap, __half* __restrict__ o_hi,
                                                          __half* __restrict__ o_lo, float s_code) {
-  constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, D = 1024, PP = HD + 4;  // PP: padded row pitch
-  __shared__ __align__(16) float qs[CH][PP], ks[CTX][PP], rk[PL][PP];
+  constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, NB = 40, D = 1024, PP = HD + 4;  // PP: padded row pitch
+  constexpr int NW = 4;  // warps, one 32-dim slice each in the dot phase
+  __shared__ __align__(16) float qs[CH][PP];
+  // ks rows [0, 24) keys, [24, 37) relative keys, [37, 40) zero; after the dot
+  // phase the same storage holds the warps' partial sums red[NW][CH][NB]
+  __shared__ __align__(16) float ks[NB * PP];
   __shared__ __align__(16) float vs[CTX][HD];
-  __shared__ float dk[CH][CTX], dr[CH][PL], wt[CH][CTX];
+  __shared__ __align__(16) float wt[CH][CTX];
+  static_assert(NW * CH * NB <= NB * PP, "partial sums alias the key rows");
   const int head = blockIdx.y;
   const int clip = blk_clip[blockIdx.x], blk = blk_index[blockIdx.x];
   const long r0 = row0[clip];
@@ -146,47 +156,65 @@ __global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict
       qv[qi] = qi < nq ? __ldg(qkv + (r0 + blk * CH + qi) * (3 * D) + head * HD + t) : 0.f;
 #pragma unroll
     for (int c = 0; c < CTX; ++c) {
-      ks[c][t] = kv[c] * kscale;
+      ks[c * PP + t] = kv[c] * kscale;
       vs[c][t] = vv[c];
     }
 #pragma unroll
-    for (int r = 0; r < PL; ++r) rk[r][t] = rv[r];
+    for (int r = 0; r < PL; ++r) ks[(CTX + r) * PP + t] = rv[r];
+#pragma unroll
+    for (int r = CTX + PL; r < NB; ++r) ks[r * PP + t] = 0.f;
 #pragma unroll
     for (int qi = 0; qi < CH; ++qi) qs[qi][t] = qv[qi] * qm;
-  }
-  __syncthreads();
-  // dot products: items [0, 288) query-key, [288, 444) query-relative
-  for (int it = t; it < CH * CTX + CH * PL; it += 128) {
-    const bool isk = it < CH * CTX;
-    const int qi = isk ? it / CTX : (it - CH * CTX) / PL;
-    const int c = isk ? it % CTX : (it - CH * CTX) % PL;
-    if (qi >= nq) continue;
-    const float4* a = reinterpret_cast<const float4*>(qs[qi]);
-    const float4* b = reinterpret_cast<const float4*>(isk ? ks[c] : rk[c]);
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;  // four independent chains
-#pragma unroll 8
-    for (int j = 0; j < HD / 4; ++j) {
-      const float4 x = a[j], y = b[j];
-      s0 = fmaf(x.x, y.x, s0);
-      s1 = fmaf(x.y, y.y, s1);
-      s2 = fmaf(x.z, y.z, s2);
-      s3 = fmaf(x.w, y.w, s3);
-    }
-    const float s = (s0 + s1) + (s2 + s3);
-    if (isk) dk[qi][c] = s;
-    else dr[qi][c] = s;
   }
   for (int i = t; i < CH * CTX; i += 128) wt[i / CTX][i % CTX] = 0.f;
   __syncthreads();
   const int lane = t & 31, warp = t >> 5;
-  for (int qi = warp; qi < nq; qi += 4) {
+  {
+    const int qg = lane & 3, cg = lane >> 2;
+    float acc[3][5];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+      for (int c = 0; c < 5; ++c) acc[i][c] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int d = warp * 32 + 4 * j;
+      float4 x[3], y[5];
+#pragma unroll
+      for (int i = 0; i < 3; ++i) x[i] = *reinterpret_cast<const float4*>(&qs[3 * qg + i][d]);
+#pragma unroll
+      for (int c = 0; c < 5; ++c) y[c] = *reinterpret_cast<const float4*>(&ks[(5 * cg + c) * PP + d]);
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int c = 0; c < 5; ++c) {
+          acc[i][c] = fmaf(x[i].x, y[c].x, acc[i][c]);
+          acc[i][c] = fmaf(x[i].y, y[c].y, acc[i][c]);
+          acc[i][c] = fmaf(x[i].z, y[c].z, acc[i][c]);
+          acc[i][c] = fmaf(x[i].w, y[c].w, acc[i][c]);
+        }
+    }
+    __syncthreads();  // every warp is done reading ks before it turns into red
+    float* red = ks + warp * (CH * NB);
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+      for (int c = 0; c < 5; ++c) red[(3 * qg + i) * NB + 5 * cg + c] = acc[i][c];
+  }
+  __syncthreads();
+  for (int qi = warp; qi < nq; qi += NW) {
     const int src = blk * CH + lane - (CTX - CH);
     const bool kv_ok = lane < CTX && src >= 0 && src < nr;
     const int rel = lane - qi;
     const bool rel_ok = lane < CTX && rel >= 0 && rel < PL;
     float sc = -INFINITY;
     if (lane < CTX) {
-      const float p = (kv_ok ? dk[qi][lane] : 0.f) + (rel_ok ? dr[qi][rel] : 0.f);
+      float p = 0.f;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) {
+        const float* red = ks + w * (CH * NB) + qi * NB;
+        p += (kv_ok ? red[lane] : 0.f) + (rel_ok ? red[CTX + rel] : 0.f);
+      }
       sc = tanhf(p / softcap) * softcap;
     }
     const float mx = warp_max_a(sc);
@@ -200,10 +228,18 @@ __global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict
 #pragma unroll
   for (int qi = 0; qi < CH; ++qi) acc[qi] = 0.f;
 #pragma unroll
-  for (int c = 0; c < CTX; ++c) {
-    const float v = vs[c][t];
+  for (int c4 = 0; c4 < CTX / 4; ++c4) {
+    float v[4];
 #pragma unroll
-    for (int qi = 0; qi < CH; ++qi) acc[qi] = fmaf(wt[qi][c], v, acc[qi]);
+    for (int u = 0; u < 4; ++u) v[u] = vs[4 * c4 + u][t];
+#pragma unroll
+    for (int qi = 0; qi < CH; ++qi) {
+      const float4 w = *reinterpret_cast<const float4*>(&wt[qi][4 * c4]);
+      acc[qi] = fmaf(w.x, v[0], acc[qi]);
+      acc[qi] = fmaf(w.y, v[1], acc[qi]);
+      acc[qi] = fmaf(w.z, v[2], acc[qi]);
+      acc[qi] = fmaf(w.w, v[3], acc[qi]);
+    }
   }
 #pragma unroll
   for (int qi = 0; qi < CH; ++qi) {
@@ -236,64 +272,171 @@ cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const fl
 // clip (runAudioDepthwiseCausalConv1dCpu, src/audio/kernels.ts:855-884),
 // conv_norm RMSNorm, SiLU (runSiluActivationCpu) -> fp16 hi/lo operand of
 // linear_end (integer codes when s_code, linear_end's input scale, is non-zero).
-// One warp per row, d = 1024.  dw: [5][1024] (tap-major).
+// Persistent blocks (two per SM, 256 threads) walk chunks of 8 packed rows.
+// A chunk and its 4-row causal halo are 12 consecutive input rows, fetched by
+// one thread as bulk copies into a double-buffered shared-memory ring, so the
+// next chunk streams in while this one is computed:
+//   conv     thread t owns channels [4t, 4t + 4): a 5-row register window
+//            slides down the chunk; row i's result overwrites its own slot,
+//            which no later row reads; per-row sums of squares meet in `red`
+//   output   warp w takes row w: conv_norm, SiLU, operand planes
+// Every wait is bounded; all threads agree on the outcome before going on.
+// dw: [5][1024] (tap-major).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) lconv_kernel(const float* __restrict__ g, const float* __restrict__ dw,
-                                                    const float* __restrict__ nw, const int* __restrict__ row_clip,
-                                                    const int* __restrict__ row0, long nrows, float eps,
-                                                    __half* __restrict__ a_hi, __half* __restrict__ a_lo,
-                                                    float s_code) {
-  constexpr int D = 1024, V = D / 128, KS = 5;
-  const int lane = threadIdx.x & 31;
-  const long row = (long)blockIdx.x * 8 + (threadIdx.x >> 5);
-  if (row >= nrows) return;
-  const long local = row - row0[row_clip[row]];
-  float4 acc[V];
-#pragma unroll
-  for (int i = 0; i < V; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-  for (int k = 0; k < KS; ++k) {
-    const long src = local + k - (KS - 1);
-    if (src < 0) continue;
-    const float4* x = reinterpret_cast<const float4*>(g + (row + k - (KS - 1)) * D);
-    const float4* wk = reinterpret_cast<const float4*>(dw + k * D);
-#pragma unroll
-    for (int i = 0; i < V; ++i) {
-      const float4 v = x[lane + 32 * i];
-      const float4 w = __ldg(wk + lane + 32 * i);
-      acc[i].x = fmaf(v.x, w.x, acc[i].x);
-      acc[i].y = fmaf(v.y, w.y, acc[i].y);
-      acc[i].z = fmaf(v.z, w.z, acc[i].z);
-      acc[i].w = fmaf(v.w, w.w, acc[i].w);
+constexpr int kLcRows = 8, kLcHalo = 4, kLcWin = kLcRows + kLcHalo, kLcD = 1024;
+constexpr int kLcStage = kLcWin * kLcD * 4;  // 48 KB
+constexpr int kLcSmem = 2 * kLcStage;
+
+__global__ void __launch_bounds__(256, 2) lconv_kernel(const float* __restrict__ g, const float* __restrict__ dw,
+                                                       const float* __restrict__ nw, const int* __restrict__ row_clip,
+                                                       const int* __restrict__ row0, long nrows, float eps,
+                                                       __half* __restrict__ a_hi, __half* __restrict__ a_lo,
+                                                       float s_code, int* err) {
+  constexpr int D = kLcD, KS = kLcHalo + 1, R = kLcRows;
+  extern __shared__ __align__(128) float lc_buf[];  // [2][12][1024]
+  __shared__ __align__(8) uint64_t bar_full[2];
+  __shared__ int first_tap[R];  // first tap whose source row lies inside the row's clip
+  __shared__ __align__(16) float red[R][8];
+  __shared__ int abort_flag, skip;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const long nchunks = (nrows + R - 1) / R;
+  if (t == 0) {
+    skip = *reinterpret_cast<volatile int*>(err) != 0;
+    abort_flag = 0;
+    mbar_init(&bar_full[0], 1);
+    mbar_init(&bar_full[1], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (skip) return;  // an earlier kernel on this device already failed
+  auto issue = [&](long chunk, int s) {
+    const long first = chunk * R - kLcHalo;
+    const long lo = first > 0 ? first : 0, hi = chunk * R + R < nrows ? chunk * R + R : nrows;
+    float* dst = lc_buf + (long)s * kLcWin * D + (lo - first) * D;
+    mbar_expect_tx(&bar_full[s], (uint32_t)((hi - lo) * D * 4));
+    for (long r = lo; r < hi; ++r) bulk_load(dst + (r - lo) * D, g + r * D, D * 4, &bar_full[s]);
+  };
+  long issued = 0;
+  if (t == 0) {
+    for (int j = 0; j < 2; ++j) {
+      const long c = blockIdx.x + (long)j * gridDim.x;
+      if (c < nchunks) {
+        issue(c, j);
+        ++issued;
+      }
     }
   }
-  float ss = 0.f;
+  float4 w[KS], nv[8];
 #pragma unroll
-  for (int i = 0; i < V; ++i) ss += acc[i].x * acc[i].x + acc[i].y * acc[i].y + acc[i].z * acc[i].z + acc[i].w * acc[i].w;
-  const float inv = 1.0f / sqrtf(warp_sum_a(ss) / (float)D + eps);
+  for (int k = 0; k < KS; ++k) w[k] = __ldg(reinterpret_cast<const float4*>(dw + k * D) + t);
+#pragma unroll
+  for (int v = 0; v < 8; ++v) nv[v] = __ldg(reinterpret_cast<const float4*>(nw) + lane + 32 * v);
   const float inv_code = s_code != 0.0f ? 1.0f / s_code : 0.0f;
-  const float4* w = reinterpret_cast<const float4*>(nw);
-#pragma unroll
-  for (int i = 0; i < V; ++i) {
-    const float4 wv = w[lane + 32 * i];
-    float v[4] = {(acc[i].x * inv) * wv.x, (acc[i].y * inv) * wv.y, (acc[i].z * inv) * wv.z, (acc[i].w * inv) * wv.w};
-    __align__(8) __half hh[4], ll[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const float s = v[u] / (1.0f + expf(-v[u]));
-      if (s_code != 0.0f) hh[u] = __float2half_rn(srq_code(s, s_code, inv_code));
-      else split_f16(s, hh[u], ll[u]);
+  long j = 0;
+  for (long chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x, ++j) {
+    const int s = (int)(j & 1);
+    const long base = chunk * R;
+    if (t < R) {
+      const long r = base + t;
+      const long local = r < nrows ? r - row0[row_clip[r]] : kLcHalo;
+      first_tap[t] = local >= kLcHalo ? 0 : (int)(kLcHalo - local);
     }
-    const int c = 4 * (lane + 32 * i);
-    *reinterpret_cast<uint2*>(a_hi + row * D + c) = *reinterpret_cast<uint2*>(hh);
-    if (s_code == 0.0f) *reinterpret_cast<uint2*>(a_lo + row * D + c) = *reinterpret_cast<uint2*>(ll);
+    const bool got = mbar_wait(&bar_full[s], (uint32_t)((j >> 1) & 1), err, kErrWaitFull, &abort_flag);
+    if (!__syncthreads_and(got)) break;
+    float* B = lc_buf + (long)s * kLcWin * D;
+    {
+      float4 win[KS];
+#pragma unroll
+      for (int k = 0; k < KS - 1; ++k) win[k] = reinterpret_cast<const float4*>(B + k * D)[t];
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        win[KS - 1] = reinterpret_cast<const float4*>(B + (i + KS - 1) * D)[t];
+        const int k0 = first_tap[i];
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < KS; ++k) {
+          if (k < k0) continue;
+          acc.x = fmaf(win[k].x, w[k].x, acc.x);
+          acc.y = fmaf(win[k].y, w[k].y, acc.y);
+          acc.z = fmaf(win[k].z, w[k].z, acc.z);
+          acc.w = fmaf(win[k].w, w[k].w, acc.w);
+        }
+        reinterpret_cast<float4*>(B + i * D)[t] = acc;
+        const float ss = warp_sum_a(acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w);
+        if (lane == 0) red[i][warp] = ss;
+#pragma unroll
+        for (int k = 0; k < KS - 1; ++k) win[k] = win[k + 1];
+      }
+    }
+    __syncthreads();
+    {
+      const long row = base + warp;
+      if (row < nrows) {
+        const float4 p0 = *reinterpret_cast<const float4*>(&red[warp][0]);
+        const float4 p1 = *reinterpret_cast<const float4*>(&red[warp][4]);
+        const float tot = ((p0.x + p0.y) + (p0.z + p0.w)) + ((p1.x + p1.y) + (p1.z + p1.w));
+        const float inv = 1.0f / sqrtf(tot / (float)D + eps);
+        const float4* xr = reinterpret_cast<const float4*>(B + warp * D);
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const float4 x = xr[lane + 32 * v];
+          float u4[4] = {(x.x * inv) * nv[v].x, (x.y * inv) * nv[v].y, (x.z * inv) * nv[v].z, (x.w * inv) * nv[v].w};
+          __align__(8) __half hh[4], ll[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const float sv = u4[u] * sigmoid_f(u4[u]);
+            if (s_code != 0.0f) hh[u] = __float2half_rn(srq_code(sv, s_code, inv_code));
+            else split_f16(sv, hh[u], ll[u]);
+          }
+          const int c = 4 * (lane + 32 * v);
+          *reinterpret_cast<uint2*>(a_hi + row * D + c) = *reinterpret_cast<uint2*>(hh);
+          if (s_code == 0.0f) *reinterpret_cast<uint2*>(a_lo + row * D + c) = *reinterpret_cast<uint2*>(ll);
+        }
+      }
+    }
+    __syncthreads();  // the stage and `red` are free again
+    if (t == 0) {
+      const long nxt = chunk + 2L * gridDim.x;
+      if (nxt < nchunks) {
+        fence_proxy_async_smem();  // this CTA's generic writes to the stage come before the copy's
+        issue(nxt, s);
+        ++issued;
+      }
+    }
+  }
+  if (t == 0) {  // after an abort: wait (bounded) for copies still in flight before the CTA exits
+    for (long q = j; q < issued; ++q) {
+      const uint32_t b = smem_u32(&bar_full[q & 1]);
+      const long long t0 = clock64();
+      while (!mbar_try_wait(b, (uint32_t)((q >> 1) & 1))) {
+        if (clock64() - t0 > kWaitCycles) {
+          atomicCAS(err, 0, kErrWaitDrain);
+          break;
+        }
+      }
+    }
   }
 }
 
 cudaError_t audio_lconv_rows(const float* g, const float* dw, const float* nw, const int* row_clip, const int* row0,
-                             long rows, float eps, __half* a_hi, __half* a_lo, float s_code, cudaStream_t st) {
+                             long rows, float eps, __half* a_hi, __half* a_lo, float s_code, int* err,
+                             cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  lconv_kernel<<<(int)((rows + 7) / 8), 256, 0, st>>>(g, dw, nw, row_clip, row0, rows, eps, a_hi, a_lo, s_code);
+  static bool attr_set[64] = {false};
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(lconv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kLcSmem);
+    if (e != cudaSuccess) return e;
+    cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (sms[dev] <= 0) sms[dev] = 148;
+    attr_set[dev] = true;
+  }
+  const long chunks = (rows + kLcRows - 1) / kLcRows;
+  const int grid = (int)(chunks < 2L * sms[dev] ? chunks : 2L * sms[dev]);
+  lconv_kernel<<<grid, 256, kLcSmem, st>>>(g, dw, nw, row_clip, row0, rows, eps, a_hi, a_lo, s_code, err);
   return cudaGetLastError();
 }
 

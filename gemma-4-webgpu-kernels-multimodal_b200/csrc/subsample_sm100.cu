@@ -5,7 +5,7 @@
 //
 // Layer 0 (1 -> 128 channels, 3x3 stride 2, channel LayerNorm with weight,
 // ReLU): one CTA per (layer-0 row, clip), one warp per frequency, lane =
-// channels lane + 32 j; statistics are warp reductions in double.  The result
+// channels 4 lane .. 4 lane + 3; statistics are warp reductions in double.  The result
 // is stored as fp16 hi / lo planes [rows][64 freq][128 ch] in which every
 // clip's rows are preceded and followed by a zero row, so a layer-1 tap that
 // leaves the clip reads zeros.
@@ -18,8 +18,9 @@
 // tile L0[2 t1 + kt - 1][2 f1 + kf - 1][c] is one dense box (64 channels x 32
 // frequencies x 4 rows at fixed parities) landing in the 128-byte swizzled
 // K-major layout the MMA reads (frequency -1 is an out-of-range, zero-filled
-// coordinate).  Operands are fp16 hi / lo planes, three terms
-// (Ah Bh + Ah Bl + Al Bh) accumulate in f32 in TMEM.  The epilogue thread of
+// coordinate).  Operands are fp16 hi / lo planes; the three terms
+// Ah Bh + Ah Bl + Al Bh accumulate in f32 in TMEM as two MMAs per k-step,
+// Ah [Bh | Bl] (N = 64) and Al Bh (N = 32).  The epilogue thread of
 // position (t1, f1) holds its 32 channels, so the LayerNorm is thread-local
 // (double statistics, as the reference's JS numbers).
 //   warp 0  TMA producer (3-stage ring)   warp 1  TMEM owner + MMA issuer
@@ -46,6 +47,16 @@ __device__ __forceinline__ void tma_load_5d(void* dst, const CUtensorMap* map, u
           "r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
+}
+
+// 1 / sqrt(a) for a normal positive double: the float hardware estimate
+// refined by two Newton-Raphson steps r <- r (3 - a r^2) / 2 in double
+// (relative error ~2^-22 -> ~2^-43 -> below double rounding).
+__device__ __forceinline__ double rsqrt_nr(double a) {
+  double r = (double)rsqrtf((float)a);
+  r = r * (1.5 - 0.5 * a * r * r);
+  r = r * (1.5 - 0.5 * a * r * r);
+  return r;
 }
 
 __device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity, int* err) {
@@ -89,46 +100,61 @@ __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restri
   }
   __syncthreads();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  float w[4][9], nw[4];
+  // lane owns channels 4 lane .. 4 lane + 3: its 36 weights are 9 float4 of w0 [128][9]
+  float w[4][9];
+  {
+    const float4* wv = reinterpret_cast<const float4*>(w0 + 36 * lane);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-#pragma unroll
-    for (int k = 0; k < 9; ++k) w[j][k] = __ldg(w0 + (lane + 32 * j) * 9 + k);
-    nw[j] = __ldg(n0 + lane + 32 * j);
+    for (int i = 0; i < 9; ++i) {
+      const float4 q = __ldg(wv + i);
+      w[(4 * i) / 9][(4 * i) % 9] = q.x;
+      w[(4 * i + 1) / 9][(4 * i + 1) % 9] = q.y;
+      w[(4 * i + 2) / 9][(4 * i + 2) % 9] = q.z;
+      w[(4 * i + 3) / 9][(4 * i + 3) % 9] = q.w;
+    }
   }
+  const float4 nq = __ldg(reinterpret_cast<const float4*>(n0) + lane);
+  const double nw[4] = {(double)nq.x, (double)nq.y, (double)nq.z, (double)nq.w};
   const long row = (long)t0off[clip] + t0;
   for (int f0 = warp; f0 < 64; f0 += 8) {
-    float v[4];
+    float x[9];
+#pragma unroll
+    for (int kt = 0; kt < 3; ++kt)
+#pragma unroll
+      for (int kf = 0; kf < 3; ++kf) {
+        const int sf = 2 * f0 + kf - 1;
+        x[kt * 3 + kf] = sf >= 0 ? xs[kt][sf] : 0.f;  // sf <= 127 always
+      }
+    double v[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float s = 0.f;
 #pragma unroll
-      for (int kt = 0; kt < 3; ++kt)
-#pragma unroll
-        for (int kf = 0; kf < 3; ++kf) {
-          const int sf = 2 * f0 + kf - 1;
-          if (sf >= 0 && sf < 128) s = fmaf(xs[kt][sf], w[j][kt * 3 + kf], s);
-        }
-      v[j] = s;
+      for (int k = 0; k < 9; ++k) s = fmaf(x[k], w[j][k], s);
+      v[j] = (double)s;
     }
-    double sum = (double)v[0] + (double)v[1] + (double)v[2] + (double)v[3];
+    double sum = (v[0] + v[1]) + (v[2] + v[3]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const double mean = sum / 128.0;
+    const double mean = sum * (1.0 / 128.0);
     double var = 0.0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) var += ((double)v[j] - mean) * ((double)v[j] - mean);
+    for (int j = 0; j < 4; ++j) var += (v[j] - mean) * (v[j] - mean);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-    const double inv = 1.0 / sqrt(var / 128.0 + (double)eps);
+    const double inv = rsqrt_nr(var * (1.0 / 128.0) + (double)eps);
+    float y[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const double y = ((double)v[j] - mean) * inv * (double)nw[j];
-      __half h, l;
-      split_f16(y > 0.0 ? (float)y : 0.f, h, l);
-      l0h[row * L0_ROW + f0 * 128 + lane + 32 * j] = h;
-      l0l[row * L0_ROW + f0 * 128 + lane + 32 * j] = l;
+      const double yd = (v[j] - mean) * inv * nw[j];
+      y[j] = yd > 0.0 ? (float)yd : 0.f;
     }
+    uint32_t h01, l01, h23, l23;
+    split2_f16(y[0], y[1], h01, l01);
+    split2_f16(y[2], y[3], h23, l23);
+    const long o = row * L0_ROW + f0 * 128 + 4 * lane;
+    *reinterpret_cast<uint2*>(l0h + o) = make_uint2(h01, h23);
+    *reinterpret_cast<uint2*>(l0l + o) = make_uint2(l01, l23);
   }
 }
 
@@ -160,7 +186,7 @@ __global__ void __launch_bounds__(SUB_THREADS, 1)
   }
   __syncthreads();
   if (skip) return;  // an earlier kernel on this device already failed
-  if (warp == 1) tmem_alloc(&tmem_slot, 32);
+  if (warp == 1) tmem_alloc(&tmem_slot, 64);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -192,19 +218,21 @@ __global__ void __launch_bounds__(SUB_THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(128, 32);
+      // B hi (32 rows) and B lo (32 rows) are adjacent 1024-byte-aligned row
+      // groups of one stage, i.e. one N = 64 operand [Bh | Bl]: columns 0..31
+      // collect Ah Bh + Al Bh, columns 32..63 Ah Bl.
+      constexpr uint32_t idesc64 = idesc_f16_f32(128, 64), idesc32 = idesc_f16_f32(128, 32);
       for (int kb = 0; kb < SKB; ++kb) {
         const int s = kb % SSTAGES;
         if (!mbar_wait(&bar_full[s], (kb / SSTAGES) & 1, err, kErrWaitFull, &abort_flag)) break;
         tc_fence_after();
         const uint32_t ah = smem_u32(sA(s, 0)), al = smem_u32(sA(s, 1));
-        const uint32_t bh = smem_u32(sB(s, 0)), bl = smem_u32(sB(s, 1));
+        const uint32_t bh = smem_u32(sB(s, 0));
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const uint64_t dah = desc_k_sw128(ah + k * 32), dbh = desc_k_sw128(bh + k * 32);
-          mma_f16_ss(tmem, dah, dbh, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          mma_f16_ss(tmem, dah, desc_k_sw128(bl + k * 32), idesc, 1u);
-          mma_f16_ss(tmem, desc_k_sw128(al + k * 32), dbh, idesc, 1u);
+          const uint64_t dbh = desc_k_sw128(bh + k * 32);
+          mma_f16_ss(tmem, desc_k_sw128(ah + k * 32), dbh, idesc64, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_f16_ss(tmem, desc_k_sw128(al + k * 32), dbh, idesc32, 1u);
         }
         mma_commit(&bar_empty[s]);
       }
@@ -216,8 +244,11 @@ __global__ void __launch_bounds__(SUB_THREADS, 1)
     const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_acc, 0, err, kErrWaitAccFull, &abort_flag));
     if (ok) {
       tc_fence_after();
-      float acc[32];
+      float acc[32], acc_lo[32];
       tmem_ld32(tmem + ((uint32_t)(32 * q) << 16), acc);
+      tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + 32, acc_lo);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] += acc_lo[j];
       const int t1 = t1_0 + q;
       if (t1 < R) {
         double mean = 0.0;  // channelValues is a Float32Array: statistics in double
@@ -255,7 +286,7 @@ __global__ void __launch_bounds__(SUB_THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 32);
+    tmem_dealloc(tmem, 64);
   }
 }
 
