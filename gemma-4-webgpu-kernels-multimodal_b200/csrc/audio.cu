@@ -386,7 +386,8 @@ static void next_scales(RowArgs& r, const float* s, int n, __half* a_c) {
 }
 
 // Row metadata of a packed batch: clip of every row, first row and row count
-// of every clip, attention blocks (clip, block of 12 rows).
+// of every clip, attention runs (clip, first of up to kAudioAttnRun blocks
+// of 12 rows).
 static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out, int* nblocks, cudaStream_t st,
                             HostKeep* keep = nullptr) {
   const int n = (int)rows.size();
@@ -396,7 +397,7 @@ static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out
   for (int i = 0; i < n; ++i) {
     row0[i] = (int)M;
     M += rows[i];
-    for (int b = 0; b < (rows[i] + 11) / 12; ++b) {
+    for (int b = 0; b < (rows[i] + 11) / 12; b += kAudioAttnRun) {
       bclip.push_back(i);
       bidx.push_back(b);
     }

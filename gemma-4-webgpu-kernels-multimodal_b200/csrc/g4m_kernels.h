@@ -148,8 +148,12 @@ cudaError_t audio_subsample_tc(const float* feats, const int* frame_off, const i
                                const float* w0, const float* n0, const __half* w1_hi, const __half* w1_lo,
                                const float* n1, float eps, __half* l0h, __half* l0l, __half* a_hi, __half* a_lo,
                                int* err, cudaStream_t st);
-cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
-                                   const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
+// Chunked audio attention over runs of up to kAudioAttnRun consecutive
+// 12-row blocks: run i covers blocks [run_blk0[i], +kAudioAttnRun) of clip
+// run_clip[i], clipped to the clip's block count.
+constexpr int kAudioAttnRun = 8;
+cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* run_clip,
+                                   const int* run_blk0, int nruns, const int* row0, const int* rows, float kscale,
                                    float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st);
 cudaError_t audio_lconv_rows(const float* g, const float* dw, const float* nw, const int* row_clip, const int* row0,
                              long rows, float eps, __half* a_hi, __half* a_lo, float s_code, int* err,

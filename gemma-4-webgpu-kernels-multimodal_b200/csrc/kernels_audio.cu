@@ -101,9 +101,11 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 // 24 (12 past-horizon rows), 13 relative positions, per-dim softplus query
 // scale, tanh softcap.  Out-of-clip context rows add no key term and no
 // value, but their slot stays in the softmax with the relative-only score.
-// One CTA per (clip block of 12 rows, head), 128 threads:
-//   stage    the 24-row key / value window (keys pre-scaled), the 13
-//            relative keys and the block's 12 scaled queries in shared memory
+// One CTA per (run of up to kAudioAttnRun consecutive 12-row blocks of one
+// clip, head), 128 threads.  The 13 relative keys are staged once; a block's
+// 12 query / key / value rows are prefetched into registers (thread = head
+// dim) while the previous block computes, and after each block its key and
+// value rows shift down to become the next block's past window:
 //   dots     the 12 x 40 products of the queries with [24 keys | 13 relative
 //            keys | 3 zero rows] as a register-blocked tile product: warp w
 //            takes dims [32w, 32w + 32), lane (qg, cg) = (lane & 3, lane >> 2)
@@ -117,152 +119,169 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 // qkv: [rows][3 * 1024] f32 (q | k | v); relk: [13][1024]; qmul: [128]
 // (= 128^-0.5 / ln 2 * softplus(per_dim_scale)); kscale = ln(1 + e) / ln 2.
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(128) audio_attn_kernel(const float* __restrict__ qkv, const float* __restrict__ relk,
-                                                         const float* __restrict__ qmul, const int* __restrict__ blk_clip,
-                                                         const int* __restrict__ blk_index,
-                                                         const int* __restrict__ row0, const int* __restrict__ rows,
-                                                         float kscale, float softcap, __half* __restrict__ o_hi,
-                                                         __half* __restrict__ o_lo, float s_code) {
+__global__ void __launch_bounds__(128, 4) audio_attn_kernel(const float* __restrict__ qkv,
+                                                            const float* __restrict__ relk,
+                                                            const float* __restrict__ qmul,
+                                                            const int* __restrict__ run_clip,
+                                                            const int* __restrict__ run_blk0,
+                                                            const int* __restrict__ row0, const int* __restrict__ rows,
+                                                            float kscale, float softcap, __half* __restrict__ o_hi,
+                                                            __half* __restrict__ o_lo, float s_code) {
   constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, NB = 40, D = 1024, PP = HD + 4;  // PP: padded row pitch
   constexpr int NW = 4;  // warps, one 32-dim slice each in the dot phase
-  __shared__ __align__(16) float qs[CH][PP];
-  // ks rows [0, 24) keys, [24, 37) relative keys, [37, 40) zero; after the dot
-  // phase the same storage holds the warps' partial sums red[NW][CH][NB]
+  // qr: the block's queries [12][PP] in the dot phase, then the warps'
+  // partial sums red[NW][12][NB] until the softmax is done
+  __shared__ __align__(16) float qr[NW * CH * NB];
+  // ks rows [0, 12) the previous block's keys, [12, 24) this block's,
+  // [24, 37) relative keys, [37, 40) zero
   __shared__ __align__(16) float ks[NB * PP];
   __shared__ __align__(16) float vs[CTX][HD];
   __shared__ __align__(16) float wt[CH][CTX];
-  static_assert(NW * CH * NB <= NB * PP, "partial sums alias the key rows");
+  static_assert(NW * CH * NB >= CH * PP, "partial sums alias the queries");
   const int head = blockIdx.y;
-  const int clip = blk_clip[blockIdx.x], blk = blk_index[blockIdx.x];
+  const int clip = run_clip[blockIdx.x], b0 = run_blk0[blockIdx.x];
   const long r0 = row0[clip];
   const int nr = rows[clip];
-  const int nq = min(CH, nr - blk * CH);  // query rows of this block
-  const int t = threadIdx.x;  // staging: thread = head dim, every row's load in flight at once
-  {
-    const float qm = qmul[t];
-    float kv[CTX], vv[CTX], rv[PL], qv[CH];
+  const int b1 = min(b0 + kAudioAttnRun, (nr + CH - 1) / CH);
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const float qm = qmul[t];
+  const float* col = qkv + r0 * (3 * D) + head * HD + t;  // this thread's dim of row 0's q
 #pragma unroll
-    for (int c = 0; c < CTX; ++c) {
-      const int src = blk * CH + c - (CTX - CH);
-      const bool ok = src >= 0 && src < nr;
-      const float* row = qkv + (r0 + (ok ? src : 0)) * (3 * D) + head * HD + t;
-      kv[c] = ok ? __ldg(row + D) : 0.f;
-      vv[c] = ok ? __ldg(row + 2 * D) : 0.f;
-    }
+  for (int r = 0; r < PL; ++r) ks[(CTX + r) * PP + t] = __ldg(relk + r * D + head * HD + t);
 #pragma unroll
-    for (int r = 0; r < PL; ++r) rv[r] = __ldg(relk + r * D + head * HD + t);
+  for (int r = CTX + PL; r < NB; ++r) ks[r * PP + t] = 0.f;
 #pragma unroll
-    for (int qi = 0; qi < CH; ++qi)
-      qv[qi] = qi < nq ? __ldg(qkv + (r0 + blk * CH + qi) * (3 * D) + head * HD + t) : 0.f;
-#pragma unroll
-    for (int c = 0; c < CTX; ++c) {
-      ks[c * PP + t] = kv[c] * kscale;
-      vs[c][t] = vv[c];
-    }
-#pragma unroll
-    for (int r = 0; r < PL; ++r) ks[(CTX + r) * PP + t] = rv[r];
-#pragma unroll
-    for (int r = CTX + PL; r < NB; ++r) ks[r * PP + t] = 0.f;
-#pragma unroll
-    for (int qi = 0; qi < CH; ++qi) qs[qi][t] = qv[qi] * qm;
+  for (int c = 0; c < CH; ++c) {  // the past window of block b0 (rows of block b0 - 1; none before row 0)
+    const int src = b0 * CH - CH + c;
+    const bool ok = src >= 0;
+    ks[c * PP + t] = ok ? __ldg(col + (long)src * (3 * D) + D) * kscale : 0.f;
+    vs[c][t] = ok ? __ldg(col + (long)src * (3 * D) + 2 * D) : 0.f;
   }
-  for (int i = t; i < CH * CTX; i += 128) wt[i / CTX][i % CTX] = 0.f;
-  __syncthreads();
-  const int lane = t & 31, warp = t >> 5;
-  {
-    const int qg = lane & 3, cg = lane >> 2;
-    float acc[3][5];
+  float pq[CH], pk[CH], pv[CH];  // the next block's rows, in flight while the current one computes
+  auto prefetch = [&](int b) {
 #pragma unroll
-    for (int i = 0; i < 3; ++i)
+    for (int i = 0; i < CH; ++i) {
+      const int src = b * CH + i;
+      const bool ok = src < nr;
+      const float* p = col + (long)(ok ? src : 0) * (3 * D);
+      pq[i] = ok ? __ldg(p) : 0.f;
+      pk[i] = ok ? __ldg(p + D) : 0.f;
+      pv[i] = ok ? __ldg(p + 2 * D) : 0.f;
+    }
+  };
+  prefetch(b0);
+  const float inv_code = s_code != 0.0f ? 1.0f / s_code : 0.0f;
+  for (int b = b0; b < b1; ++b) {
 #pragma unroll
-      for (int c = 0; c < 5; ++c) acc[i][c] = 0.f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int d = warp * 32 + 4 * j;
-      float4 x[3], y[5];
-#pragma unroll
-      for (int i = 0; i < 3; ++i) x[i] = *reinterpret_cast<const float4*>(&qs[3 * qg + i][d]);
-#pragma unroll
-      for (int c = 0; c < 5; ++c) y[c] = *reinterpret_cast<const float4*>(&ks[(5 * cg + c) * PP + d]);
+    for (int i = 0; i < CH; ++i) {
+      qr[i * PP + t] = pq[i] * qm;
+      ks[(CH + i) * PP + t] = pk[i] * kscale;
+      vs[CH + i][t] = pv[i];
+    }
+    for (int i = t; i < CH * CTX; i += 128) wt[i / CTX][i % CTX] = 0.f;
+    __syncthreads();
+    if (b + 1 < b1) prefetch(b + 1);
+    const int nq = min(CH, nr - b * CH);  // query rows of this block
+    {
+      const int qg = lane & 3, cg = lane >> 2;
+      float acc[3][5];
 #pragma unroll
       for (int i = 0; i < 3; ++i)
 #pragma unroll
-        for (int c = 0; c < 5; ++c) {
-          acc[i][c] = fmaf(x[i].x, y[c].x, acc[i][c]);
-          acc[i][c] = fmaf(x[i].y, y[c].y, acc[i][c]);
-          acc[i][c] = fmaf(x[i].z, y[c].z, acc[i][c]);
-          acc[i][c] = fmaf(x[i].w, y[c].w, acc[i][c]);
-        }
-    }
-    __syncthreads();  // every warp is done reading ks before it turns into red
-    float* red = ks + warp * (CH * NB);
+        for (int c = 0; c < 5; ++c) acc[i][c] = 0.f;
 #pragma unroll
-    for (int i = 0; i < 3; ++i)
+      for (int j = 0; j < 8; ++j) {
+        const int d = warp * 32 + 4 * j;
+        float4 x[3], y[5];
 #pragma unroll
-      for (int c = 0; c < 5; ++c) red[(3 * qg + i) * NB + 5 * cg + c] = acc[i][c];
-  }
-  __syncthreads();
-  for (int qi = warp; qi < nq; qi += NW) {
-    const int src = blk * CH + lane - (CTX - CH);
-    const bool kv_ok = lane < CTX && src >= 0 && src < nr;
-    const int rel = lane - qi;
-    const bool rel_ok = lane < CTX && rel >= 0 && rel < PL;
-    float sc = -INFINITY;
-    if (lane < CTX) {
-      float p = 0.f;
+        for (int i = 0; i < 3; ++i) x[i] = *reinterpret_cast<const float4*>(&qr[(3 * qg + i) * PP + d]);
 #pragma unroll
-      for (int w = 0; w < NW; ++w) {
-        const float* red = ks + w * (CH * NB) + qi * NB;
-        p += (kv_ok ? red[lane] : 0.f) + (rel_ok ? red[CTX + rel] : 0.f);
+        for (int c = 0; c < 5; ++c) y[c] = *reinterpret_cast<const float4*>(&ks[(5 * cg + c) * PP + d]);
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+          for (int c = 0; c < 5; ++c) {
+            acc[i][c] = fmaf(x[i].x, y[c].x, acc[i][c]);
+            acc[i][c] = fmaf(x[i].y, y[c].y, acc[i][c]);
+            acc[i][c] = fmaf(x[i].z, y[c].z, acc[i][c]);
+            acc[i][c] = fmaf(x[i].w, y[c].w, acc[i][c]);
+          }
       }
-      sc = tanhf(p / softcap) * softcap;
+      __syncthreads();  // every warp is done reading the queries before they turn into red
+      float* red = qr + warp * (CH * NB);
+#pragma unroll
+      for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int c = 0; c < 5; ++c) red[(3 * qg + i) * NB + 5 * cg + c] = acc[i][c];
     }
-    const float mx = warp_max_a(sc);
-    const float e = lane < CTX ? expf(sc - mx) : 0.f;
-    const float den = warp_sum_a(e);
-    if (lane < CTX) wt[qi][lane] = kv_ok ? e / den : 0.f;  // out-of-clip slots add no value
-  }
-  __syncthreads();
-  const float inv_code = s_code != 0.0f ? 1.0f / s_code : 0.0f;
-  float acc[CH];  // the 12 rows' sums as independent chains (rows >= nq have zero weights)
+    __syncthreads();
+    for (int qi = warp; qi < nq; qi += NW) {
+      const int src = b * CH + lane - (CTX - CH);
+      const bool kv_ok = lane < CTX && src >= 0 && src < nr;
+      const int rel = lane - qi;
+      const bool rel_ok = lane < CTX && rel >= 0 && rel < PL;
+      float sc = -INFINITY;
+      if (lane < CTX) {
+        float p = 0.f;
 #pragma unroll
-  for (int qi = 0; qi < CH; ++qi) acc[qi] = 0.f;
+        for (int w = 0; w < NW; ++w) {
+          const float* red = qr + w * (CH * NB) + qi * NB;
+          p += (kv_ok ? red[lane] : 0.f) + (rel_ok ? red[CTX + rel] : 0.f);
+        }
+        sc = tanhf(p / softcap) * softcap;
+      }
+      const float mx = warp_max_a(sc);
+      const float e = lane < CTX ? expf(sc - mx) : 0.f;
+      const float den = warp_sum_a(e);
+      if (lane < CTX) wt[qi][lane] = kv_ok ? e / den : 0.f;  // out-of-clip slots add no value
+    }
+    __syncthreads();
+    float acc[CH];  // the 12 rows' sums as independent chains (rows >= nq have zero weights)
 #pragma unroll
-  for (int c4 = 0; c4 < CTX / 4; ++c4) {
-    float v[4];
+    for (int qi = 0; qi < CH; ++qi) acc[qi] = 0.f;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = vs[4 * c4 + u][t];
+    for (int c4 = 0; c4 < CTX / 4; ++c4) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = vs[4 * c4 + u][t];
+#pragma unroll
+      for (int qi = 0; qi < CH; ++qi) {
+        const float4 w = *reinterpret_cast<const float4*>(&wt[qi][4 * c4]);
+        acc[qi] = fmaf(w.x, v[0], acc[qi]);
+        acc[qi] = fmaf(w.y, v[1], acc[qi]);
+        acc[qi] = fmaf(w.z, v[2], acc[qi]);
+        acc[qi] = fmaf(w.w, v[3], acc[qi]);
+      }
+    }
 #pragma unroll
     for (int qi = 0; qi < CH; ++qi) {
-      const float4 w = *reinterpret_cast<const float4*>(&wt[qi][4 * c4]);
-      acc[qi] = fmaf(w.x, v[0], acc[qi]);
-      acc[qi] = fmaf(w.y, v[1], acc[qi]);
-      acc[qi] = fmaf(w.z, v[2], acc[qi]);
-      acc[qi] = fmaf(w.w, v[3], acc[qi]);
+      if (qi >= nq) break;
+      const float o = acc[qi];
+      const long oi = (r0 + b * CH + qi) * D + head * HD + t;
+      if (s_code != 0.0f) {  // integer codes for the post projection's input scale
+        o_hi[oi] = __float2half_rn(srq_code(o, s_code, inv_code));
+      } else {
+        __half h, l;
+        split_f16(o, h, l);
+        o_hi[oi] = h;
+        o_lo[oi] = l;
+      }
     }
-  }
+    __syncthreads();  // every read of this block's window is done
 #pragma unroll
-  for (int qi = 0; qi < CH; ++qi) {
-    if (qi >= nq) break;
-    const float o = acc[qi];
-    const long oi = (r0 + blk * CH + qi) * D + head * HD + t;
-    if (s_code != 0.0f) {  // integer codes for the post projection's input scale
-      o_hi[oi] = __float2half_rn(srq_code(o, s_code, inv_code));
-    } else {
-      __half h, l;
-      split_f16(o, h, l);
-      o_hi[oi] = h;
-      o_lo[oi] = l;
+    for (int i = 0; i < CH; ++i) {  // this block's keys and values become the next block's past (own column)
+      ks[i * PP + t] = ks[(CH + i) * PP + t];
+      vs[i][t] = vs[CH + i][t];
     }
   }
 }
 
-cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* blk_clip,
-                                   const int* blk_index, int nblocks, const int* row0, const int* rows, float kscale,
+cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const float* qmul, const int* run_clip,
+                                   const int* run_blk0, int nruns, const int* row0, const int* rows, float kscale,
                                    float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st) {
-  if (nblocks <= 0) return cudaSuccess;
-  dim3 grid(nblocks, 8);
-  audio_attn_kernel<<<grid, 128, 0, st>>>(qkv, relk, qmul, blk_clip, blk_index, row0, rows, kscale, softcap, o_hi,
+  if (nruns <= 0) return cudaSuccess;
+  dim3 grid(nruns, 8);
+  audio_attn_kernel<<<grid, 128, 0, st>>>(qkv, relk, qmul, run_clip, run_blk0, row0, rows, kscale, softcap, o_hi,
                                           o_lo, s_code);
   return cudaGetLastError();
 }
