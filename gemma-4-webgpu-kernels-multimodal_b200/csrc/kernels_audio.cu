@@ -102,23 +102,60 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 // scale, tanh softcap.  Out-of-clip context rows add no key term and no
 // value, but their slot stays in the softmax with the relative-only score.
 // One CTA per (run of up to kAudioAttnRun consecutive 12-row blocks of one
-// clip, head), 128 threads.  The 13 relative keys are staged once; a block's
-// 12 query / key / value rows are prefetched into registers (thread = head
-// dim) while the previous block computes, and after each block its key and
-// value rows shift down to become the next block's past window:
-//   dots     the 12 x 40 products of the queries with [24 keys | 13 relative
-//            keys | 3 zero rows] as a register-blocked tile product: warp w
-//            takes dims [32w, 32w + 32), lane (qg, cg) = (lane & 3, lane >> 2)
-//            a 3 x 5 block of rows 3qg.. and slots 5cg..; each float4 step
-//            loads 8 vectors (broadcast, bank-conflict free with the 132-float
-//            row pitch) for 60 FMAs; the 4 warps' partial sums meet in the
-//            softmax
+// clip, head), 128 threads.  Both products run on the tensor cores as
+// mma.sync m16n8k16 (f16 in, f32 accumulate) over split operands: every
+// f32 value x is stored as hi = f16(x) and lo = f16((x - hi) 2^11), and
+// x y = hi_x hi_y + 2^-11 (hi_x lo_y + lo_x hi_y) to ~22 bits, the scaled
+// residual never entering the f16 subnormal range.
+//   stage    the block's 12 query / key / value rows are prefetched into
+//            registers (thread = head dim) while the previous block computes;
+//            keys and values go to a two-slot ring (the previous block's rows
+//            stay in the other slot), values transposed [dim][slot row]; the
+//            13 relative keys are staged once per CTA
+//   scores   [12 (16) queries] x [24 keys | 13 relative keys | 3 zero] over
+//            128 dims: warp w takes dims [32w, 32w + 32); partial sums meet in
+//            the softmax
 //   softmax  one warp per query row, lane = context slot: tanh softcap, max,
-//            exp, sum; weights of out-of-clip slots kept in the denominator
-//   P*V      thread = output dim, 24-term sums for each of the 12 rows
+//            exp, sum; weights of out-of-clip slots kept in the denominator;
+//            P written as hi / lo planes in ring order
+//   P*V      [16 x 32 ring slots] x [32 x 128]: warp w takes dims [32w, +32)
 // qkv: [rows][3 * 1024] f32 (q | k | v); relk: [13][1024]; qmul: [128]
 // (= 128^-0.5 / ln 2 * softplus(per_dim_scale)); kscale = ln(1 + e) / ln 2.
 // ---------------------------------------------------------------------------
+namespace {
+constexpr int kAtQP = 136;  // halves per query / key row (68 words: fragment loads hit 32 distinct banks)
+constexpr int kAtVP = 40;   // halves per transposed value row and per P row (20 words)
+constexpr int kAtQBytes = 2 * 16 * kAtQP * 2;       // Qh, Ql [16][136]
+constexpr int kAtRedBytes = 4 * 12 * 40 * 4;        // red [4 warps][12][40] f32, aliases the queries
+constexpr int kAtKBytes = 2 * 40 * kAtQP * 2;       // Kh, Kl [40][136]
+constexpr int kAtVBytes = 2 * 128 * kAtVP * 2;      // Vth, Vtl [128][40]
+constexpr int kAtPBytes = 2 * 16 * kAtVP * 2;       // Ph, Pl [16][40]
+constexpr int kAtSmem = (kAtQBytes > kAtRedBytes ? kAtQBytes : kAtRedBytes) + kAtKBytes + kAtVBytes + kAtPBytes;
+constexpr float kLoScale = 2048.0f, kLoInv = 1.0f / 2048.0f;
+
+__device__ __forceinline__ void split_scaled(float x, __half& hi, __half& lo) {
+  hi = __float2half_rn(x);
+  lo = __float2half_rn((x - __half2float(hi)) * kLoScale);
+}
+
+// tanh(x) = sign(x) (1 - 2 / (2^(2 |x| log2 e) + 1)), absolute error ~1e-7;
+// saturates to +-1 without overflow.
+__device__ __forceinline__ float tanh_f(float x) {
+  const float e = ex2_approx(2.0f * kLog2eF * fabsf(x));
+  return copysignf(1.0f - 2.0f * rcp_approx(e + 1.0f), x);
+}
+
+__device__ __forceinline__ uint32_t ld_h2(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+__device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+}  // namespace
+
 __global__ void __launch_bounds__(128, 4) audio_attn_kernel(const float* __restrict__ qkv,
                                                             const float* __restrict__ relk,
                                                             const float* __restrict__ qmul,
@@ -127,152 +164,226 @@ __global__ void __launch_bounds__(128, 4) audio_attn_kernel(const float* __restr
                                                             const int* __restrict__ row0, const int* __restrict__ rows,
                                                             float kscale, float softcap, __half* __restrict__ o_hi,
                                                             __half* __restrict__ o_lo, float s_code) {
-  constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, NB = 40, D = 1024, PP = HD + 4;  // PP: padded row pitch
-  constexpr int NW = 4;  // warps, one 32-dim slice each in the dot phase
-  // qr: the block's queries [12][PP] in the dot phase, then the warps'
-  // partial sums red[NW][12][NB] until the softmax is done
-  __shared__ __align__(16) float qr[NW * CH * NB];
-  // ks rows [0, 12) the previous block's keys, [12, 24) this block's,
-  // [24, 37) relative keys, [37, 40) zero
-  __shared__ __align__(16) float ks[NB * PP];
-  __shared__ __align__(16) float vs[CTX][HD];
-  __shared__ __align__(16) float wt[CH][CTX];
-  static_assert(NW * CH * NB >= CH * PP, "partial sums alias the queries");
+  constexpr int HD = 128, CH = 12, CTX = 24, PL = 13, NB = 40, D = 1024, NW = 4;
+  extern __shared__ __align__(16) uint8_t at_smem[];
+  __half* Qh = reinterpret_cast<__half*>(at_smem);
+  __half* Ql = Qh + 16 * kAtQP;
+  float* red = reinterpret_cast<float*>(at_smem);  // [NW][CH][NB], after the score MMAs
+  uint8_t* p8 = at_smem + (kAtQBytes > kAtRedBytes ? kAtQBytes : kAtRedBytes);
+  __half* Kh = reinterpret_cast<__half*>(p8);  // rows: ring slots [0, 24), relative keys [24, 37), zero [37, 40)
+  __half* Kl = Kh + 40 * kAtQP;
+  __half* Vth = Kl + 40 * kAtQP;  // [dim][ring slot], slots [24, 40) zero
+  __half* Vtl = Vth + 128 * kAtVP;
+  __half* Ph = Vtl + 128 * kAtVP;  // [query][ring slot]
+  __half* Pl = Ph + 16 * kAtVP;
+
   const int head = blockIdx.y;
   const int clip = run_clip[blockIdx.x], b0 = run_blk0[blockIdx.x];
   const long r0 = row0[clip];
   const int nr = rows[clip];
   const int b1 = min(b0 + kAudioAttnRun, (nr + CH - 1) / CH);
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+  const int g = lane >> 2, tig = lane & 3;
+  const __half hz = __float2half_rn(0.f);
+  // zero what no block writes: query rows 12..15, key rows 37..39, P, the value slots 24..39
+  for (int i = t; i < 2 * 4 * kAtQP; i += 128) (i < 4 * kAtQP ? Qh : Ql)[12 * kAtQP + (i % (4 * kAtQP))] = hz;
+  for (int i = t; i < 2 * 3 * kAtQP; i += 128) (i < 3 * kAtQP ? Kh : Kl)[37 * kAtQP + (i % (3 * kAtQP))] = hz;
+  for (int i = t; i < 2 * 16 * kAtVP; i += 128) Ph[i] = hz;  // Ph and Pl are contiguous
+  for (int i = t; i < 2 * 128 * kAtVP; i += 128) Vth[i] = hz;  // Vth and Vtl are contiguous
+  __syncthreads();
   const float qm = qmul[t];
   const float* col = qkv + r0 * (3 * D) + head * HD + t;  // this thread's dim of row 0's q
 #pragma unroll
-  for (int r = 0; r < PL; ++r) ks[(CTX + r) * PP + t] = __ldg(relk + r * D + head * HD + t);
+  for (int r = 0; r < PL; ++r) {
+    __half h, l;
+    split_scaled(__ldg(relk + r * D + head * HD + t), h, l);
+    Kh[(CTX + r) * kAtQP + t] = h;
+    Kl[(CTX + r) * kAtQP + t] = l;
+  }
+  {  // the past window of block b0 (rows of block b0 - 1; none before row 0) in the slot block b0 does not use
+    const int slot = 12 * (1 - (b0 & 1));
 #pragma unroll
-  for (int r = CTX + PL; r < NB; ++r) ks[r * PP + t] = 0.f;
-#pragma unroll
-  for (int c = 0; c < CH; ++c) {  // the past window of block b0 (rows of block b0 - 1; none before row 0)
-    const int src = b0 * CH - CH + c;
-    const bool ok = src >= 0;
-    ks[c * PP + t] = ok ? __ldg(col + (long)src * (3 * D) + D) * kscale : 0.f;
-    vs[c][t] = ok ? __ldg(col + (long)src * (3 * D) + 2 * D) : 0.f;
+    for (int c = 0; c < CH; ++c) {
+      const int src = b0 * CH - CH + c;
+      const bool ok = src >= 0;
+      __half h, l;
+      split_scaled(ok ? __ldg(col + (long)src * (3 * D) + D) * kscale : 0.f, h, l);
+      Kh[(slot + c) * kAtQP + t] = h;
+      Kl[(slot + c) * kAtQP + t] = l;
+      split_scaled(ok ? __ldg(col + (long)src * (3 * D) + 2 * D) : 0.f, h, l);
+      Vth[t * kAtVP + slot + c] = h;
+      Vtl[t * kAtVP + slot + c] = l;
+    }
   }
   float pq[CH], pk[CH], pv[CH];  // the next block's rows, in flight while the current one computes
   auto prefetch = [&](int b) {
+    const float* p = col + (long)(b * CH) * (3 * D);  // row b * 12; rows i at constant offsets
+    const int n = nr - b * CH;                        // rows of block b inside the clip
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
-      const int src = b * CH + i;
-      const bool ok = src < nr;
-      const float* p = col + (long)(ok ? src : 0) * (3 * D);
-      pq[i] = ok ? __ldg(p) : 0.f;
-      pk[i] = ok ? __ldg(p + D) : 0.f;
-      pv[i] = ok ? __ldg(p + 2 * D) : 0.f;
+      pq[i] = pk[i] = pv[i] = 0.f;
+      if (i < n) {
+        pq[i] = __ldg(p + i * (3 * D));
+        pk[i] = __ldg(p + i * (3 * D) + D);
+        pv[i] = __ldg(p + i * (3 * D) + 2 * D);
+      }
     }
   };
   prefetch(b0);
   const float inv_code = s_code != 0.0f ? 1.0f / s_code : 0.0f;
+  const float inv_cap = 1.0f / softcap;
   for (int b = b0; b < b1; ++b) {
+    const int cur = 12 * (b & 1), prev = 12 - cur;  // ring slots of this block's rows and of the past window
 #pragma unroll
     for (int i = 0; i < CH; ++i) {
-      qr[i * PP + t] = pq[i] * qm;
-      ks[(CH + i) * PP + t] = pk[i] * kscale;
-      vs[CH + i][t] = pv[i];
+      __half h, l;
+      split_scaled(pq[i] * qm, h, l);
+      Qh[i * kAtQP + t] = h;
+      Ql[i * kAtQP + t] = l;
+      split_scaled(pk[i] * kscale, h, l);
+      Kh[(cur + i) * kAtQP + t] = h;
+      Kl[(cur + i) * kAtQP + t] = l;
     }
-    for (int i = t; i < CH * CTX; i += 128) wt[i / CTX][i % CTX] = 0.f;
+#pragma unroll
+    for (int i = 0; i < CH; i += 2) {
+      const __half2 h2 = __floats2half2_rn(pv[i], pv[i + 1]);
+      const float2 back = __half22float2(h2);
+      *reinterpret_cast<__half2*>(Vth + t * kAtVP + cur + i) = h2;
+      *reinterpret_cast<__half2*>(Vtl + t * kAtVP + cur + i) =
+          __floats2half2_rn((pv[i] - back.x) * kLoScale, (pv[i + 1] - back.y) * kLoScale);
+    }
     __syncthreads();
     if (b + 1 < b1) prefetch(b + 1);
     const int nq = min(CH, nr - b * CH);  // query rows of this block
     {
-      const int qg = lane & 3, cg = lane >> 2;
-      float acc[3][5];
+      // scores: context slot c -> key row (c < 12: past window, c < 24: this block, else relative / zero)
+      int krow[5];
 #pragma unroll
-      for (int i = 0; i < 3; ++i)
+      for (int nt = 0; nt < 5; ++nt) {
+        const int c = nt * 8 + g;
+        krow[nt] = c < CH ? prev + c : (c < CTX ? cur + c - CH : c);
+      }
+      float hh[5][4], xx[5][4];
 #pragma unroll
-        for (int c = 0; c < 5; ++c) acc[i][c] = 0.f;
+      for (int nt = 0; nt < 5; ++nt)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int d = warp * 32 + 4 * j;
-        float4 x[3], y[5];
+        for (int u = 0; u < 4; ++u) hh[nt][u] = xx[nt][u] = 0.f;
 #pragma unroll
-        for (int i = 0; i < 3; ++i) x[i] = *reinterpret_cast<const float4*>(&qr[(3 * qg + i) * PP + d]);
+      for (int j = 0; j < 2; ++j) {
+        const int kb = warp * 32 + 16 * j + 2 * tig;
+        uint32_t ah[4], al[4];
+        ah[0] = ld_h2(Qh + g * kAtQP + kb);
+        ah[1] = ld_h2(Qh + (g + 8) * kAtQP + kb);
+        ah[2] = ld_h2(Qh + g * kAtQP + kb + 8);
+        ah[3] = ld_h2(Qh + (g + 8) * kAtQP + kb + 8);
+        al[0] = ld_h2(Ql + g * kAtQP + kb);
+        al[1] = ld_h2(Ql + (g + 8) * kAtQP + kb);
+        al[2] = ld_h2(Ql + g * kAtQP + kb + 8);
+        al[3] = ld_h2(Ql + (g + 8) * kAtQP + kb + 8);
 #pragma unroll
-        for (int c = 0; c < 5; ++c) y[c] = *reinterpret_cast<const float4*>(&ks[(5 * cg + c) * PP + d]);
-#pragma unroll
-        for (int i = 0; i < 3; ++i)
-#pragma unroll
-          for (int c = 0; c < 5; ++c) {
-            acc[i][c] = fmaf(x[i].x, y[c].x, acc[i][c]);
-            acc[i][c] = fmaf(x[i].y, y[c].y, acc[i][c]);
-            acc[i][c] = fmaf(x[i].z, y[c].z, acc[i][c]);
-            acc[i][c] = fmaf(x[i].w, y[c].w, acc[i][c]);
-          }
+        for (int nt = 0; nt < 5; ++nt) {
+          const __half* kh = Kh + krow[nt] * kAtQP + kb;
+          const __half* kl = Kl + krow[nt] * kAtQP + kb;
+          const uint32_t bh0 = ld_h2(kh), bh1 = ld_h2(kh + 8), bl0 = ld_h2(kl), bl1 = ld_h2(kl + 8);
+          mma_16816(hh[nt], ah, bh0, bh1);
+          mma_16816(xx[nt], ah, bl0, bl1);
+          mma_16816(xx[nt], al, bh0, bh1);
+        }
       }
       __syncthreads();  // every warp is done reading the queries before they turn into red
-      float* red = qr + warp * (CH * NB);
+      float* rw = red + warp * (CH * NB);
 #pragma unroll
-      for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int c = 0; c < 5; ++c) red[(3 * qg + i) * NB + 5 * cg + c] = acc[i][c];
+      for (int nt = 0; nt < 5; ++nt) {
+        const int cc = nt * 8 + 2 * tig;
+        *reinterpret_cast<float2*>(rw + g * NB + cc) =
+            make_float2(fmaf(xx[nt][0], kLoInv, hh[nt][0]), fmaf(xx[nt][1], kLoInv, hh[nt][1]));
+        if (g + 8 < CH)
+          *reinterpret_cast<float2*>(rw + (g + 8) * NB + cc) =
+              make_float2(fmaf(xx[nt][2], kLoInv, hh[nt][2]), fmaf(xx[nt][3], kLoInv, hh[nt][3]));
+      }
     }
     __syncthreads();
-    for (int qi = warp; qi < nq; qi += NW) {
+    for (int qi = warp; qi < CH; qi += NW) {
       const int src = b * CH + lane - (CTX - CH);
       const bool kv_ok = lane < CTX && src >= 0 && src < nr;
       const int rel = lane - qi;
       const bool rel_ok = lane < CTX && rel >= 0 && rel < PL;
       float sc = -INFINITY;
-      if (lane < CTX) {
+      if (lane < CTX && qi < nq) {
         float p = 0.f;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
-          const float* red = qr + w * (CH * NB) + qi * NB;
-          p += (kv_ok ? red[lane] : 0.f) + (rel_ok ? red[CTX + rel] : 0.f);
+          const float* rr = red + w * (CH * NB) + qi * NB;
+          p += (kv_ok ? rr[lane] : 0.f) + (rel_ok ? rr[CTX + rel] : 0.f);
         }
-        sc = tanhf(p / softcap) * softcap;
+        sc = tanh_f(p * inv_cap) * softcap;
       }
       const float mx = warp_max_a(sc);
-      const float e = lane < CTX ? expf(sc - mx) : 0.f;
-      const float den = warp_sum_a(e);
-      if (lane < CTX) wt[qi][lane] = kv_ok ? e / den : 0.f;  // out-of-clip slots add no value
+      const float e = (lane < CTX && qi < nq) ? ex2_approx((sc - mx) * kLog2eF) : 0.f;
+      const float inv_den = rcp_approx(warp_sum_a(e));
+      if (lane < CTX) {
+        // out-of-clip slots add no value; rows past the clip end get zero weights
+        const float wgt = (kv_ok && qi < nq) ? e * inv_den : 0.f;
+        const int slot = lane < CH ? prev + lane : cur + lane - CH;
+        __half h, l;
+        split_scaled(wgt, h, l);
+        Ph[qi * kAtVP + slot] = h;
+        Pl[qi * kAtVP + slot] = l;
+      }
     }
     __syncthreads();
-    float acc[CH];  // the 12 rows' sums as independent chains (rows >= nq have zero weights)
+    {
+      float oh[4][4], ox[4][4];
 #pragma unroll
-    for (int qi = 0; qi < CH; ++qi) acc[qi] = 0.f;
+      for (int n = 0; n < 4; ++n)
 #pragma unroll
-    for (int c4 = 0; c4 < CTX / 4; ++c4) {
-      float v[4];
+        for (int u = 0; u < 4; ++u) oh[n][u] = ox[n][u] = 0.f;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = vs[4 * c4 + u][t];
+      for (int j = 0; j < 2; ++j) {
+        const int kb = 16 * j + 2 * tig;
+        uint32_t ah[4], al[4];
+        ah[0] = ld_h2(Ph + g * kAtVP + kb);
+        ah[1] = ld_h2(Ph + (g + 8) * kAtVP + kb);
+        ah[2] = ld_h2(Ph + g * kAtVP + kb + 8);
+        ah[3] = ld_h2(Ph + (g + 8) * kAtVP + kb + 8);
+        al[0] = ld_h2(Pl + g * kAtVP + kb);
+        al[1] = ld_h2(Pl + (g + 8) * kAtVP + kb);
+        al[2] = ld_h2(Pl + g * kAtVP + kb + 8);
+        al[3] = ld_h2(Pl + (g + 8) * kAtVP + kb + 8);
 #pragma unroll
-      for (int qi = 0; qi < CH; ++qi) {
-        const float4 w = *reinterpret_cast<const float4*>(&wt[qi][4 * c4]);
-        acc[qi] = fmaf(w.x, v[0], acc[qi]);
-        acc[qi] = fmaf(w.y, v[1], acc[qi]);
-        acc[qi] = fmaf(w.z, v[2], acc[qi]);
-        acc[qi] = fmaf(w.w, v[3], acc[qi]);
+        for (int n = 0; n < 4; ++n) {
+          const int dim = warp * 32 + n * 8 + g;
+          const __half* vh = Vth + dim * kAtVP + kb;
+          const __half* vl = Vtl + dim * kAtVP + kb;
+          const uint32_t bh0 = ld_h2(vh), bh1 = ld_h2(vh + 8), bl0 = ld_h2(vl), bl1 = ld_h2(vl + 8);
+          mma_16816(oh[n], ah, bh0, bh1);
+          mma_16816(ox[n], ah, bl0, bl1);
+          mma_16816(ox[n], al, bh0, bh1);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int dim = head * HD + warp * 32 + n * 8 + 2 * tig;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int qi = g + 8 * half;
+          if (qi >= nq) continue;
+          const float o0 = fmaf(ox[n][2 * half], kLoInv, oh[n][2 * half]);
+          const float o1 = fmaf(ox[n][2 * half + 1], kLoInv, oh[n][2 * half + 1]);
+          const long oi = (r0 + b * CH + qi) * D + dim;
+          if (s_code != 0.0f) {  // integer codes for the post projection's input scale
+            *reinterpret_cast<__half2*>(o_hi + oi) = __halves2half2(
+                __float2half_rn(srq_code(o0, s_code, inv_code)), __float2half_rn(srq_code(o1, s_code, inv_code)));
+          } else {
+            uint32_t hv, lv;
+            split2_f16(o0, o1, hv, lv);
+            *reinterpret_cast<uint32_t*>(o_hi + oi) = hv;
+            *reinterpret_cast<uint32_t*>(o_lo + oi) = lv;
+          }
+        }
       }
     }
-#pragma unroll
-    for (int qi = 0; qi < CH; ++qi) {
-      if (qi >= nq) break;
-      const float o = acc[qi];
-      const long oi = (r0 + b * CH + qi) * D + head * HD + t;
-      if (s_code != 0.0f) {  // integer codes for the post projection's input scale
-        o_hi[oi] = __float2half_rn(srq_code(o, s_code, inv_code));
-      } else {
-        __half h, l;
-        split_f16(o, h, l);
-        o_hi[oi] = h;
-        o_lo[oi] = l;
-      }
-    }
-    __syncthreads();  // every read of this block's window is done
-#pragma unroll
-    for (int i = 0; i < CH; ++i) {  // this block's keys and values become the next block's past (own column)
-      ks[i * PP + t] = ks[(CH + i) * PP + t];
-      vs[i][t] = vs[CH + i][t];
-    }
+    __syncthreads();  // P and the value ring are free for the next block
   }
 }
 
@@ -280,8 +391,17 @@ cudaError_t audio_attention_blocks(const float* qkv, const float* relk, const fl
                                    const int* run_blk0, int nruns, const int* row0, const int* rows, float kscale,
                                    float softcap, __half* o_hi, __half* o_lo, float s_code, cudaStream_t st) {
   if (nruns <= 0) return cudaSuccess;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(audio_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmem);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
   dim3 grid(nruns, 8);
-  audio_attn_kernel<<<grid, 128, 0, st>>>(qkv, relk, qmul, run_clip, run_blk0, row0, rows, kscale, softcap, o_hi,
+  audio_attn_kernel<<<grid, 128, kAtSmem, st>>>(qkv, relk, qmul, run_clip, run_blk0, row0, rows, kscale, softcap, o_hi,
                                           o_lo, s_code);
   return cudaGetLastError();
 }
