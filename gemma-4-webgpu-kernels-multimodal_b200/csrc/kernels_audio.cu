@@ -24,20 +24,45 @@ __device__ __forceinline__ float warp_max_a(float v) {
 // ---------------------------------------------------------------------------
 // Log-mel front end: preprocessGemma4AudioSamples (src/preprocess/audio.ts:22-118)
 // for unpadded clips: periodic Hann window (320), zero-padded radix-2 FFT
-// (512), magnitude, HTK mel filters (257 x 128), log(mel + 1e-3).  One CTA
-// (256 threads) per frame.  Frame f of a clip reads waveform samples
-// [f*160 - 160, f*160 + 160) (160 leading zeros, frameLength / 2).
+// (512), magnitude, HTK mel filters (257 x 128), log(mel + 1e-3).  Frame f
+// of a clip reads waveform samples [f*160 - 160, f*160 + 160) (160 leading
+// zeros, frameLength / 2).
+//
+// One warp per frame, 8 frames per 256-thread CTA.  The 512 points live in
+// registers, 16 per lane: butterfly stages of half-size 1..8 run inside a
+// lane in the blocked layout (element 16 lane + j), half-size 16 pairs lanes
+// lane ^ 1 through shuffles, a padded shared-memory transpose moves to the
+// cyclic layout (element lane + 32 j), where half-sizes 32..256 again run
+// inside a lane.  Every butterfly is fftRadix2's (src/preprocess/audio.ts:
+// 191-212): double arithmetic from float inputs, without contraction, stored
+// to float as its Float32Array is.
 // ---------------------------------------------------------------------------
+namespace {
+__device__ __forceinline__ void fft_bfly(float& er, float& ei, float& odr, float& odi, double wr, double wi) {
+  const double xr = odr, xi = odi;
+  const double tr = __dsub_rn(__dmul_rn(xr, wr), __dmul_rn(xi, wi));
+  const double ti = __dadd_rn(__dmul_rn(xr, wi), __dmul_rn(xi, wr));
+  const double a = er, b = ei;
+  odr = (float)__dsub_rn(a, tr);
+  odi = (float)__dsub_rn(b, ti);
+  er = (float)__dadd_rn(a, tr);
+  ei = (float)__dadd_rn(b, ti);
+}
+}  // namespace
+
 __global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ samples, const long* __restrict__ soff,
                                                      const long* __restrict__ slen, const int* __restrict__ foff,
-                                                     const int* __restrict__ fcount, int clips,
+                                                     const int* __restrict__ fcount, int clips, int total_frames,
                                                      const float* __restrict__ window, const float* __restrict__ mel,
                                                      const int* __restrict__ mel_rng, const double2* __restrict__ tw,
                                                      float* __restrict__ feats) {
-  __shared__ float re[512], im[512], mag[257];
-  const int gf = blockIdx.x;
-  // clip of this frame: binary search over frame offsets
-  int lo = 0, hi = clips - 1;
+  constexpr int PADN = 512 + 32;  // one float2 of padding after every 16 elements
+  __shared__ float2 xb[8][PADN];
+  __shared__ float mg[8][260];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gf = blockIdx.x * 8 + warp;
+  if (gf >= total_frames) return;  // warp-uniform: the kernel only synchronises within a warp
+  int lo = 0, hi = clips - 1;      // clip of this frame: binary search over frame offsets
   while (lo < hi) {
     const int mid = (lo + hi + 1) >> 1;
     if (foff[mid] <= gf) lo = mid;
@@ -47,42 +72,72 @@ __global__ void __launch_bounds__(256) logmel_kernel(const float* __restrict__ s
   if (f >= fcount[clip]) return;
   const float* x = samples + soff[clip];
   const long L = slen[clip];
-  const int t = threadIdx.x;
-  // bit-reversed load (9-bit index)
-  for (int i = t; i < 512; i += 256) {
+  float re[16], im[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {  // element 16 lane + j holds input sample brev9(16 lane + j)
+    const int n = __brev(16 * lane + j) >> 23;
     float v = 0.f;
-    if (i < 320) {
-      const long idx = (long)f * 160 + i - 160;
-      if (idx >= 0 && idx < L) v = x[idx] * window[i];
+    if (n < 320) {
+      const long idx = (long)f * 160 + n - 160;
+      if (idx >= 0 && idx < L) v = x[idx] * __ldg(window + n);
     }
-    const int r = __brev(i) >> 23;
-    re[r] = v;
-    im[r] = 0.f;
+    re[j] = v;
+    im[j] = 0.f;
   }
-  __syncthreads();
-  // Butterflies in double, stored to float, as fftRadix2 does with JS
-  // numbers and Float32Array storage (src/preprocess/audio.ts:191-212).
-  for (int size = 2; size <= 512; size <<= 1) {
-    const int half = size >> 1;
-    const int g = t / half, k = t % half;
-    const int e = g * size + k, o = e + half;
-    const double2 w = tw[k * (512 / size)];  // exp(-2 pi i k / size)
-    const double orr = (double)re[o] * w.x - (double)im[o] * w.y;
-    const double oi = (double)re[o] * w.y + (double)im[o] * w.x;
-    const double er = re[e], ei = im[e];
-    re[o] = (float)(er - orr);
-    im[o] = (float)(ei - oi);
-    re[e] = (float)(er + orr);
-    im[e] = (float)(ei + oi);
-    __syncthreads();
+#pragma unroll
+  for (int st = 0; st < 4; ++st) {  // half-sizes 1, 2, 4, 8: partners in the same lane
+    const int half = 1 << st, size = 2 << st;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j & half) continue;
+      const double2 w = __ldg(tw + (j & (half - 1)) * (512 / size));  // offset in the group = j mod half
+      fft_bfly(re[j], im[j], re[j + half], im[j + half], w.x, w.y);
+    }
   }
-  for (int b = t; b < 257; b += 256) mag[b] = (float)hypot((double)re[b], (double)im[b]);
-  __syncthreads();
-  if (t < 128) {
+  {  // half-size 16: element 16 lane + j pairs with lane ^ 1; odd lanes hold the upper members
+    const bool upper = lane & 1;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const float pr = __shfl_xor_sync(0xffffffffu, re[j], 1), pim = __shfl_xor_sync(0xffffffffu, im[j], 1);
+      const double2 w = __ldg(tw + j * 16);
+      float er = upper ? pr : re[j], ei = upper ? pim : im[j];
+      float odr = upper ? re[j] : pr, odi = upper ? im[j] : pim;
+      fft_bfly(er, ei, odr, odi, w.x, w.y);
+      re[j] = upper ? odr : er;
+      im[j] = upper ? odi : ei;
+    }
+  }
+  float2* xw = xb[warp];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) xw[17 * lane + j] = make_float2(re[j], im[j]);  // p + p / 16, p = 16 lane + j
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {  // element p = lane + 32 j
+    const float2 v = xw[lane + 34 * j + (lane >> 4)];
+    re[j] = v.x;
+    im[j] = v.y;
+  }
+#pragma unroll
+  for (int st = 5; st < 9; ++st) {  // half-sizes 32 .. 256: partners j and j + half / 32 in the same lane
+    const int hj = 1 << (st - 5), half = 32 << (st - 5), size = 2 * half;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      if (j & hj) continue;
+      const int k = lane + 32 * (j & (hj - 1));  // (lane + 32 j) mod half
+      const double2 w = __ldg(tw + k * (512 / size));
+      fft_bfly(re[j], im[j], re[j + hj], im[j + hj], w.x, w.y);
+    }
+  }
+  float* mw = mg[warp];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) mw[lane + 32 * j] = (float)hypot((double)re[j], (double)im[j]);
+  if (lane == 0) mw[256] = (float)hypot((double)re[8], (double)im[8]);
+  __syncwarp();
+  for (int m = lane; m < 128; m += 32) {
     double e = 0.0;  // mel energy in double (JS number), in bin order, over the non-zero bins
-    const int b1 = mel_rng[2 * t + 1];
-    for (int b = mel_rng[2 * t]; b <= b1; ++b) e += (double)mag[b] * (double)mel[b * 128 + t];
-    feats[(long)gf * 128 + t] = (float)log(e + 0.001);
+    const int b1 = mel_rng[2 * m + 1];
+    for (int b = mel_rng[2 * m]; b <= b1; ++b) e = __dadd_rn(e, __dmul_rn((double)mw[b], (double)mel[b * 128 + m]));
+    feats[(long)gf * 128 + m] = (float)log(e + 0.001);
   }
 }
 
@@ -90,8 +145,8 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
                          const int* frames, int clips, int total_frames, const float* window, const float* mel,
                          const int* mel_rng, const double2* twiddle, float* features, cudaStream_t st) {
   if (total_frames <= 0) return cudaSuccess;
-  logmel_kernel<<<total_frames, 256, 0, st>>>(samples, sample_off, sample_len, frame_off, frames, clips, window, mel,
-                                              mel_rng, twiddle, features);
+  logmel_kernel<<<(total_frames + 7) / 8, 256, 0, st>>>(samples, sample_off, sample_len, frame_off, frames, clips,
+                                                        total_frames, window, mel, mel_rng, twiddle, features);
   return cudaGetLastError();
 }
 
