@@ -100,6 +100,24 @@ int load_audio(Device& d, const SafeTensors& f) {
   if (!ew) return rc;
   aw.c0w = up(d, c0, f);
   aw.c0n = up(d, c0n, f);
+  {  // layer-0 LayerNorm statistics from the taps: wbar_k = mean_c w[c][k], G_kl = (1 or 2) mean_c w[c][k] w[c][l]
+    const float* w = (const float*)f.data(*c0);
+    std::vector<double> stv(54, 0.0);
+    for (int k = 0; k < 9; ++k) {
+      for (int c = 0; c < 128; ++c) stv[k] += (double)w[c * 9 + k];
+      stv[k] /= 128.0;
+    }
+    int q = 9;
+    for (int k = 0; k < 9; ++k)
+      for (int l = k; l < 9; ++l) {
+        double g = 0.0;
+        for (int c = 0; c < 128; ++c) g += (double)w[c * 9 + k] * (double)w[c * 9 + l];
+        stv[q++] = (k == l ? 1.0 : 2.0) * g / 128.0;
+      }
+    aw.c0stat = (double*)dalloc(d, stv.size() * sizeof(double));
+    if (!aw.c0stat || cudaMemcpy(aw.c0stat, stv.data(), stv.size() * sizeof(double), cudaMemcpyHostToDevice))
+      return fail(G4M_E_CUDA, "audio subsample statistics upload failed");
+  }
   aw.c1n = up(d, c1n, f);
   {  // layer-1 conv as tap-major rows [kt * 3 + kf][c_out][c_in], fp16 hi / lo (the conv GEMM's B operand)
     const float* w = (const float*)f.data(*c1);
@@ -630,7 +648,7 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   __half* l0l = l0h + (size_t)T0S * 64 * 128;
   G4M_RUN("subsample", audio_subsample_tc((const float*)b.feats.p, dfoff, dfcnt, (const int*)b.t0_off.p, T0S,
                                           (const int*)b.clip_row0.p, (const int*)b.clip_rows.p, n, max_t0, max_rows,
-                                          aw.c0w, aw.c0n, aw.c1_hi, aw.c1_lo, aw.c1n, 1e-6f, l0h, l0l, ah, al, d.err,
+                                          aw.c0w, aw.c0stat, aw.c0n, aw.c1_hi, aw.c1_lo, aw.c1n, 1e-6f, l0h, l0l, ah, al, d.err,
                                           st));
   GemmArgs a = aargs(d, M, D, D);
   a.out_f32 = h;

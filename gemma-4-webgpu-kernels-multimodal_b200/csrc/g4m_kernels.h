@@ -145,9 +145,9 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 // w1_hi / w1_lo: layer-1 weights [9 taps][32 out][128 in].
 cudaError_t audio_subsample_tc(const float* feats, const int* frame_off, const int* frames, const int* t0off,
                                long l0_rows, const int* row0, const int* rows, int clips, int max_t0, int max_rows,
-                               const float* w0, const float* n0, const __half* w1_hi, const __half* w1_lo,
-                               const float* n1, float eps, __half* l0h, __half* l0l, __half* a_hi, __half* a_lo,
-                               int* err, cudaStream_t st);
+                               const float* w0, const double* w0stat, const float* n0, const __half* w1_hi,
+                               const __half* w1_lo, const float* n1, float eps, __half* l0h, __half* l0l,
+                               __half* a_hi, __half* a_lo, int* err, cudaStream_t st);
 // Chunked audio attention over runs of up to kAudioAttnRun consecutive
 // 12-row blocks: run i covers blocks [run_blk0[i], +kAudioAttnRun) of clip
 // run_clip[i], clipped to the clip's block count.

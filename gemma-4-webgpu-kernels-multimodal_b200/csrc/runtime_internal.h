@@ -82,6 +82,7 @@ struct AudioWeights {
   std::vector<AudioLayer> L;
   float* c0w = nullptr;  // [128][1][3][3]
   float* c0n = nullptr;  // [128]
+  double* c0stat = nullptr;  // layer-0 weight moments: wbar[9], then G[k][l] for k <= l (45)
   __half *c1_hi = nullptr, *c1_lo = nullptr;  // layer-1 conv [9 taps][32 out][128 in], fp16 hi / lo
   float* c1n = nullptr;  // [32]
   __half *in_hi = nullptr, *in_lo = nullptr;    // input projection [1024, 1024]

@@ -4,8 +4,8 @@
 // source times are in the reference.
 //
 // Layer 0 (1 -> 128 channels, 3x3 stride 2, channel LayerNorm with weight,
-// ReLU): one CTA per (layer-0 row, clip), one warp per frequency, lane =
-// channels 4 lane .. 4 lane + 3; statistics are warp reductions in double.  The result
+// ReLU): statistics in double from the nine taps and precomputed weight
+// moments, then one warp per (row, frequency) with lane = 4 channels.  The result
 // is stored as fp16 hi / lo planes [rows][64 freq][128 ch] in which every
 // clip's rows are preceded and followed by a zero row, so a layer-1 tap that
 // leaves the clip reads zeros.
@@ -71,88 +71,107 @@ __device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity, int
 }
 }  // namespace
 
+// Layer 0 for 4 layer-0 rows x 64 frequencies per CTA (256 (row, frequency)
+// tasks).  The LayerNorm statistics of a task follow from its nine taps x_k:
+// with v_c = sum_k x_k w[c][k], mean = sum_k x_k wbar_k and
+// E[v^2] = sum_{k<=l} x_k x_l G_kl, where wbar_k = (1/128) sum_c w[c][k] and
+// G_kl = (1 or 2)/128 sum_c w[c][k] w[c][l] (w0stat: 9 + 45 doubles), so
+// one thread per task computes them in double (54 FMAs) before the channel
+// pass.  The channel pass is one warp per task, lane = channels 4 lane ..
+// 4 lane + 3 (weights in registers), writing 256 contiguous bytes per plane.
 __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restrict__ feats, const int* __restrict__ foff,
                                                            const int* __restrict__ fcount, const int* __restrict__ t0off,
-                                                           const float* __restrict__ w0, const float* __restrict__ n0,
-                                                           float eps, __half* __restrict__ l0h,
-                                                           __half* __restrict__ l0l) {
-  __shared__ float xs[3][128];
-  const int clip = blockIdx.y, t0 = blockIdx.x;
+                                                           const float* __restrict__ w0,
+                                                           const double* __restrict__ w0stat,
+                                                           const float* __restrict__ n0, float eps,
+                                                           __half* __restrict__ l0h, __half* __restrict__ l0l) {
+  __shared__ __align__(16) float xs[9][128];  // input frames 2 rb - 1 .. 2 rb + 7
+  __shared__ double stat_s[54];
+  __shared__ __align__(16) double2 mi[256];    // (mean, 1 / sqrt(var + eps)) per task
+  const int clip = blockIdx.y, rb = blockIdx.x * 4;  // first layer-0 row of this CTA
   const int F = fcount[clip];
   const int T0 = (F - 1) / 2 + 1;
-  if (t0 > T0) return;
-  if (t0 == T0) {  // the zero row after the clip (and, for clip 0, the one before it)
-    const long r = (long)t0off[clip] + T0;
-    for (int i = threadIdx.x; i < L0_ROW; i += 256) {
-      l0h[r * L0_ROW + i] = __float2half_rn(0.f);
-      l0l[r * L0_ROW + i] = __float2half_rn(0.f);
-      if (clip == 0) {
-        l0h[(long)(t0off[0] - 1) * L0_ROW + i] = __float2half_rn(0.f);
-        l0l[(long)(t0off[0] - 1) * L0_ROW + i] = __float2half_rn(0.f);
-      }
-    }
-    return;
-  }
+  if (rb > T0) return;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const float* fx = feats + (long)foff[clip] * 128;
-  for (int i = threadIdx.x; i < 3 * 128; i += 256) {
-    const int r = 2 * t0 - 1 + i / 128;
-    xs[i / 128][i % 128] = (r >= 0 && r < F) ? fx[(long)r * 128 + (i % 128)] : 0.f;
+  for (int i = t; i < 9 * 128; i += 256) {
+    const int fr = 2 * rb - 1 + i / 128;
+    xs[i / 128][i % 128] = (fr >= 0 && fr < F) ? fx[(long)fr * 128 + (i % 128)] : 0.f;
   }
+  if (t < 54) stat_s[t] = w0stat[t];
   __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // lane owns channels 4 lane .. 4 lane + 3: its 36 weights are 9 float4 of w0 [128][9]
-  float w[4][9];
+  {  // statistics of task t = (row rb + t / 64, frequency t % 64)
+    const int rr = t >> 6, f0 = t & 63;
+    double x[9];
+#pragma unroll
+    for (int kt = 0; kt < 3; ++kt)
+#pragma unroll
+      for (int kf = 0; kf < 3; ++kf) {
+        const int sf = 2 * f0 + kf - 1;  // <= 127
+        x[kt * 3 + kf] = sf >= 0 ? (double)xs[2 * rr + kt][sf] : 0.0;
+      }
+    double mean = 0.0, e2 = 0.0;
+    int q = 9;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) {
+      mean = fma(x[k], stat_s[k], mean);
+#pragma unroll
+      for (int l = k; l < 9; ++l) e2 = fma(x[k] * x[l], stat_s[q++], e2);
+    }
+    const double var = fmax(e2 - mean * mean, 0.0);
+    mi[t] = make_double2(mean, rsqrt_nr(var + (double)eps));
+  }
+  float w[4][9];  // this lane's channels 4 lane .. 4 lane + 3: 9 float4 of w0 [128][9]
   {
     const float4* wv = reinterpret_cast<const float4*>(w0 + 36 * lane);
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
-      const float4 q = __ldg(wv + i);
-      w[(4 * i) / 9][(4 * i) % 9] = q.x;
-      w[(4 * i + 1) / 9][(4 * i + 1) % 9] = q.y;
-      w[(4 * i + 2) / 9][(4 * i + 2) % 9] = q.z;
-      w[(4 * i + 3) / 9][(4 * i + 3) % 9] = q.w;
+      const float4 q4 = __ldg(wv + i);
+      w[(4 * i) / 9][(4 * i) % 9] = q4.x;
+      w[(4 * i + 1) / 9][(4 * i + 1) % 9] = q4.y;
+      w[(4 * i + 2) / 9][(4 * i + 2) % 9] = q4.z;
+      w[(4 * i + 3) / 9][(4 * i + 3) % 9] = q4.w;
     }
   }
   const float4 nq = __ldg(reinterpret_cast<const float4*>(n0) + lane);
   const double nw[4] = {(double)nq.x, (double)nq.y, (double)nq.z, (double)nq.w};
-  const long row = (long)t0off[clip] + t0;
-  for (int f0 = warp; f0 < 64; f0 += 8) {
+  __syncthreads();
+  for (int task = warp; task < 256; task += 8) {
+    const int rr = task >> 6, f0 = task & 63, r = rb + rr;
+    if (r > T0) break;  // tasks run in row order
+    const long row = (long)t0off[clip] + r;
+    const long o = row * L0_ROW + f0 * 128 + 4 * lane;
+    if (r == T0) {  // the zero row after the clip (and, for clip 0, the one before it)
+      *reinterpret_cast<uint2*>(l0h + o) = make_uint2(0u, 0u);
+      *reinterpret_cast<uint2*>(l0l + o) = make_uint2(0u, 0u);
+      if (clip == 0) {
+        const long o0 = (long)(t0off[0] - 1) * L0_ROW + f0 * 128 + 4 * lane;
+        *reinterpret_cast<uint2*>(l0h + o0) = make_uint2(0u, 0u);
+        *reinterpret_cast<uint2*>(l0l + o0) = make_uint2(0u, 0u);
+      }
+      continue;
+    }
     float x[9];
 #pragma unroll
     for (int kt = 0; kt < 3; ++kt)
 #pragma unroll
       for (int kf = 0; kf < 3; ++kf) {
         const int sf = 2 * f0 + kf - 1;
-        x[kt * 3 + kf] = sf >= 0 ? xs[kt][sf] : 0.f;  // sf <= 127 always
+        x[kt * 3 + kf] = sf >= 0 ? xs[2 * rr + kt][sf] : 0.f;
       }
-    double v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float s = 0.f;
-#pragma unroll
-      for (int k = 0; k < 9; ++k) s = fmaf(x[k], w[j][k], s);
-      v[j] = (double)s;
-    }
-    double sum = (v[0] + v[1]) + (v[2] + v[3]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const double mean = sum * (1.0 / 128.0);
-    double var = 0.0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) var += (v[j] - mean) * (v[j] - mean);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) var += __shfl_xor_sync(0xffffffffu, var, o);
-    const double inv = rsqrt_nr(var * (1.0 / 128.0) + (double)eps);
+    const double2 s2 = mi[task];
     float y[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const double yd = (v[j] - mean) * inv * nw[j];
+      float v = 0.f;
+#pragma unroll
+      for (int k = 0; k < 9; ++k) v = fmaf(x[k], w[j][k], v);
+      const double yd = ((double)v - s2.x) * s2.y * nw[j];
       y[j] = yd > 0.0 ? (float)yd : 0.f;
     }
     uint32_t h01, l01, h23, l23;
     split2_f16(y[0], y[1], h01, l01);
     split2_f16(y[2], y[3], h23, l23);
-    const long o = row * L0_ROW + f0 * 128 + 4 * lane;
     *reinterpret_cast<uint2*>(l0h + o) = make_uint2(h01, h23);
     *reinterpret_cast<uint2*>(l0l + o) = make_uint2(l01, l23);
   }
@@ -328,9 +347,9 @@ static bool make_l0_map(CUtensorMap* map, const __half* base, long total_rows) {
 
 cudaError_t audio_subsample_tc(const float* feats, const int* frame_off, const int* frames, const int* t0off,
                                long l0_rows, const int* row0, const int* rows, int clips, int max_t0, int max_rows,
-                               const float* w0, const float* n0, const __half* w1_hi, const __half* w1_lo,
-                               const float* n1, float eps, __half* l0h, __half* l0l, __half* a_hi, __half* a_lo,
-                               int* err, cudaStream_t st) {
+                               const float* w0, const double* w0stat, const float* n0, const __half* w1_hi,
+                               const __half* w1_lo, const float* n1, float eps, __half* l0h, __half* l0l,
+                               __half* a_hi, __half* a_lo, int* err, cudaStream_t st) {
   if (clips <= 0 || max_rows <= 0) return cudaSuccess;
   if (clips > 65535) return cudaErrorInvalidValue;  // grid y = clip
   static bool attr[64] = {false};
@@ -341,7 +360,8 @@ cudaError_t audio_subsample_tc(const float* feats, const int* frame_off, const i
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  subsample_l0_kernel<<<dim3(max_t0 + 1, clips), 256, 0, st>>>(feats, frame_off, frames, t0off, w0, n0, eps, l0h, l0l);
+  subsample_l0_kernel<<<dim3((max_t0 + 1 + 3) / 4, clips), 256, 0, st>>>(feats, frame_off, frames, t0off, w0, w0stat,
+                                                                        n0, eps, l0h, l0l);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   CUtensorMap mLh, mLl, mWh, mWl;
