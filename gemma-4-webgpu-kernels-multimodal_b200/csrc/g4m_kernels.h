@@ -142,7 +142,9 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 // Subsample convs.  Layer-0 rows of clip i start at row t0off[i] of the fp16
 // hi / lo planes l0h, l0l ([l0_rows][64][128]; a zero row precedes and
 // follows every clip); output rows at packed row row0[i], rows[i] of them.
-// w1_hi / w1_lo: layer-1 weights [9 taps][32 out][128 in].
+// w0: layer-0 weights [128][9]; w0stat: their moments (wbar[9], then
+// G[k][l] for k <= l, 45 values) for the LayerNorm statistics;
+// w1_hi / w1_lo: layer-1 weights [9 taps][32 out][128 in].  (subsample_sm100.cu)
 cudaError_t audio_subsample_tc(const float* feats, const int* frame_off, const int* frames, const int* t0off,
                                long l0_rows, const int* row0, const int* rows, int clips, int max_t0, int max_rows,
                                const float* w0, const double* w0stat, const float* n0, const __half* w1_hi,

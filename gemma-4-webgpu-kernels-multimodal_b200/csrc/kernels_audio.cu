@@ -1,5 +1,6 @@
-// Audio tower kernels: log-mel front end, fused two-layer subsample conv,
-// chunked local self-attention and the light-conv depthwise block.
+// Audio tower kernels: log-mel front end, chunked local self-attention and
+// the light-conv depthwise block (the subsample convs are in
+// subsample_sm100.cu).
 //
 // Clips are packed back to back (ragged rows): clip c owns encoder rows
 // [clip_row0[c], clip_row0[c] + clip_rows[c]).  Every row-coupled kernel
