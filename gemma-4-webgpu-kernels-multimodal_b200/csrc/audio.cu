@@ -751,6 +751,32 @@ int g4m_audio_embed_device(g4m_ctx* ctx, int di, int n, const float* samples_dev
   return audio_forward(ctx, d, shapes, samples_dev, soff, sampling_rate, layer_count, out_dev, st);
 }
 
+}  // extern "C"
+
+// Chunks [first, last) of one device's clips (longest first) for the
+// pipelined batch call.  Only the first chunk's upload and the last chunk's
+// download are not hidden behind compute, so the head and the tail hold at
+// most kEdgeRows encoder rows each (37 M-tiles: a 1024-column GEMM over them
+// is one 148-tile wave), and the middle chunk takes all the rest, keeping the
+// GEMMs' tile waves full.  Batches under three edges' worth of rows run as
+// one chunk.
+static std::vector<std::pair<int, int>> audio_batch_chunks(const std::vector<ClipShape>& sh) {
+  constexpr long kEdgeRows = 37 * 128;
+  const int m = (int)sh.size();
+  long total = 0;
+  for (const ClipShape& c : sh) total += c.t1;
+  if (m < 3 || total < 3 * kEdgeRows) return {{0, m}};
+  int h = 0;
+  long rows = 0;
+  while (h < m - 2 && (h == 0 || rows + sh[h].t1 <= kEdgeRows)) rows += sh[h++].t1;
+  int t = m;
+  rows = 0;
+  while (t > h + 1 && (t == m || rows + sh[t - 1].t1 <= kEdgeRows)) rows += sh[--t].t1;
+  return {{0, h}, {h, t}, {t, m}};
+}
+
+extern "C" {
+
 int g4m_audio_embed_batch(g4m_ctx* ctx, int n, const float* const* samples, const int64_t* lengths, int sampling_rate,
                           int layer_count, int64_t max_samples, float* const* out, int* rows_out, int* status) {
   if (!ctx || n < 0 || (n > 0 && (!samples || !lengths || !out))) return fail(G4M_E_ARG, "bad argument");
@@ -798,11 +824,11 @@ int g4m_audio_embed_batch(g4m_ctx* ctx, int n, const float* const* samples, cons
     int r = G4M_OK;
     if (ensure(d.ab.samples, std::max<long>(total, 1) * 4) || ensure(d.io_out, std::max<long>(rows, 1) * 1536 * 4))
       r = fail(G4M_E_CUDA, "audio io allocation failed");
-    // chunks of ~32 clips (longest first, so the first chunk sizes the
-    // buffers): uploads queue on the copy stream, each chunk's forward waits
-    // for its upload, each download for its forward
+    // a short head and tail chunk and one middle chunk (audio_batch_chunks):
+    // uploads queue on the copy stream, each chunk's forward waits for its
+    // upload, each download for its forward
     const int m = (int)part[g].size();
-    const auto chunks = batch_chunks(m, 32);
+    const auto chunks = audio_batch_chunks(sh);
     std::vector<cudaEvent_t> up(chunks.size()), done(chunks.size());
     for (size_t c = 0; c < chunks.size(); ++c) {
       cudaEventCreateWithFlags(&up[c], cudaEventDisableTiming);
