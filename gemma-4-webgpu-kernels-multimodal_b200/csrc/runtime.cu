@@ -855,9 +855,10 @@ int g4m_vision_embed_batch(g4m_ctx* ctx, int n, const float* const* pixels, int 
     const size_t img = (size_t)height * width * 3, ob = (size_t)tokens * 1536;
     int r = G4M_OK;
     if (ensure(d.io_in, cnt * img * 4) || ensure(d.io_out, cnt * ob * 4)) r = fail(G4M_E_CUDA, "io allocation failed");
-    // chunks of ~16 images: uploads queue on the copy stream, each chunk's
-    // forward waits for its upload, each download for its forward
-    const auto chunks = batch_chunks(cnt, 16);
+    // 4-image head and tail chunks around middle chunks of <= 28 images:
+    // uploads queue on the copy stream, each chunk's forward waits for its
+    // upload, each download for its forward
+    const auto chunks = edge_chunks(cnt, 4, 28);
     std::vector<cudaEvent_t> up(chunks.size()), done(chunks.size());
     for (size_t k = 0; k < chunks.size(); ++k) {
       cudaEventCreateWithFlags(&up[k], cudaEventDisableTiming);

@@ -193,12 +193,23 @@ inline cudaError_t upload_meta(void* dst, const void* src, size_t bytes, cudaStr
   return cudaMemcpyAsync(dst, keep->bufs.back().data(), bytes, cudaMemcpyHostToDevice, st);
 }
 
-// Chunks of a batch call: [begin, end) ranges of `n` items, about `per` each,
-// so the copies of one chunk overlap the compute of another.
-inline std::vector<std::pair<int, int>> batch_chunks(int n, int per) {
+// Chunks [first, last) of n equal items for a pipelined batch call.  Only
+// the first chunk's upload and the last chunk's download are not hidden
+// behind compute, so the head and the tail hold `edge` items and the middle
+// is cut into chunks of at most `mid` items (each chunk's upload has to fit
+// under the previous chunk's compute).  Batches under three edges run as one
+// chunk.
+inline std::vector<std::pair<int, int>> edge_chunks(int n, int edge, int mid) {
   std::vector<std::pair<int, int>> c;
-  const int k = std::max(1, (n + std::max(per, 1) - 1) / std::max(per, 1));
-  for (int i = 0; i < k; ++i) c.push_back({(int)((long)n * i / k), (int)((long)n * (i + 1) / k)});
+  if (n < 3 * edge || edge <= 0 || mid <= 0) {
+    c.push_back({0, n});
+    return c;
+  }
+  c.push_back({0, edge});
+  const int body = n - 2 * edge, k = (body + mid - 1) / mid;
+  for (int i = 0; i < k; ++i)
+    c.push_back({edge + (int)((long)body * i / k), edge + (int)((long)body * (i + 1) / k)});
+  c.push_back({n - edge, n});
   return c;
 }
 
