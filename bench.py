@@ -251,15 +251,20 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     p = weights_path("audio", 12, args.quant, rank, barrier)
     ctx = ctx_cls([torch.cuda.current_device()])
     ctx.load_weights(p)
-    n = args.clips
-    lens = syn.audio_batch_lengths(1000 + rank, n)
+    # the job's world * clips clips (one seeded draw), balanced over the ranks
+    # by encoder rows with the batch call's LPT rule
+    job_lens = syn.audio_batch_lengths(1000, world * args.clips)
+    mine = sorted(sharding.lpt_assign([audio_rows(int(L)) for L in job_lens], world)[rank])
+    lens = job_lens[mine]
+    n = len(mine)
+    job_seconds = float(job_lens.sum()) / 16000.0
     total = int(lens.sum())
     host = torch.empty(total, dtype=torch.float32).pin_memory()
     offs = np.zeros(n, np.int64)
     o = 0
-    for i, L in enumerate(lens):
-        host[o:o + int(L)] = torch.from_numpy(syn.audio_samples(5000 + rank * n + i, int(L)))
-        offs[i] = o
+    for j, (i, L) in enumerate(zip(mine, lens)):
+        host[o:o + int(L)] = torch.from_numpy(syn.audio_samples(5000 + i, int(L)))
+        offs[j] = o
         o += int(L)
     dev = host.cuda()
     rows = sum(audio_rows(int(L)) for L in lens)
@@ -280,7 +285,7 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     launches = native.kernel_launches() - launches0
     ms = sharding.max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
     audio_seconds = float(lens.sum()) / 16000.0
-    value = world * audio_seconds * args.steps / (ms / 1000.0)
+    value = job_seconds * args.steps / (ms / 1000.0)
     ctx.profile_begin()
     step()
     prof = ctx.profile_end()
@@ -307,11 +312,13 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     res = {
         "metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": value, "unit": "audio-s/s",
         "ms_per_step": ms / args.steps,
-        "config": {"workload": f"batched audio: {n} clips/GPU, lengths U[1,30] s (seeded), packed rows (no padding)",
-                   "clips_per_gpu": n, "audio_seconds_per_gpu": audio_seconds, "encoder_rows_per_gpu": rows,
+        "config": {"workload": f"batched audio: {args.clips} clips/GPU, lengths U[1,30] s (seeded), packed rows "
+                               "(no padding), clips LPT-balanced over the ranks by encoder rows",
+                   "clips_per_gpu": args.clips, "clips_this_rank": n, "audio_seconds_job": job_seconds,
+                   "audio_seconds_this_rank": audio_seconds, "encoder_rows_this_rank": rows,
                    "activation_quant": QUANT_DESC[args.quant]},
         "gpu_launches": launches,
-        "e2e": {"value": world * audio_seconds * k_e2e / te, "unit": "audio-s/s",
+        "e2e": {"value": job_seconds * k_e2e / te, "unit": "audio-s/s",
                 "h2d_bytes_per_step": total * 4, "d2h_bytes_per_step": rows * 1536 * 4},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
                      "frac": ach / peak, "peak_source": "measured (bf16 cuBLAS, sustained)", "traffic": None,
