@@ -43,7 +43,9 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
   static constexpr int STAGES = (196608 / STAGE_BYTES) > 6 ? 6 : (196608 / STAGE_BYTES);
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int EPI_STAGE = 4096;  // per epilogue warp: a 32-row x 128-byte store block
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 4 * kEpiGroups * EPI_STAGE + 1024;
+  static_assert(SMEM + 1024 <= 232448, "pipeline + epilogue stages exceed 227 KB of shared memory");
   static constexpr int TMEM_COLS = 2 * BN;
 };
 
@@ -68,6 +70,36 @@ __device__ __forceinline__ void store_f16x2_row(__half* hi, __half* lo, const fl
     for (int u = 0; u < 4; ++u) split2_f16(v[j + 2 * u], v[j + 2 * u + 1], hv[u], lv[u]);
     *reinterpret_cast<uint4*>(hi + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
     *reinterpret_cast<uint4*>(lo + j) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+  }
+}
+
+// One 64-column head of the vision q | k | v projection: per-channel weight
+// scale x row scale, output srq, then the head RMSNorm (weight nw, or none
+// for v: runVisionRmsNormCpu, src/vision/kernels.ts:5-32).
+__device__ __forceinline__ void load_scales32(const float* p, float* s);
+__device__ __forceinline__ void qkv_head_norm(float* v, const float* col_scale, float rsw, float so, float eps,
+                                              const float* nw) {
+  float sc[32];
+  load_scales32(col_scale, sc);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = (v[j] * rsw) * sc[j];
+  load_scales32(col_scale + 32, sc);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[32 + j] = (v[32 + j] * rsw) * sc[j];
+  if (so != 0.0f) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = srq_f(v[j], so);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 64; ++j) ss = fmaf(v[j], v[j], ss);
+  const float inv = 1.0f / sqrtf(ss / 64.0f + eps);
+  if (nw) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = (v[j] * inv) * __ldg(nw + j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = v[j] * inv;
   }
 }
 
@@ -99,6 +131,69 @@ __device__ __forceinline__ void store_codes_row(__half* dst, const float* v, flo
       hv[u] = c.w;
     }
     *reinterpret_cast<uint4*>(dst + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+  }
+}
+
+// Warp-cooperative store of a 32-row block: block row r belongs to lane r,
+// whose RB bytes are vals[0 .. RB/16).  The rows pass through the warp's
+// shared-memory stage (16-byte slots XOR-swizzled so that both phases are
+// bank-conflict free) and leave row-contiguously, RB/16 lanes per row, so
+// every store instruction writes whole 32-byte sectors of 512/RB rows rather
+// than a 16-byte piece of each of 32 rows.  Block row r goes to
+// base + r * stride (bytes); rows r >= nrows are not written.
+template <int RB>
+__device__ __forceinline__ void warp_store_block(uint4* stage, const uint4 (&vals)[RB / 16], char* base,
+                                                 size_t stride, int nrows, int lane) {
+  constexpr int S = RB / 16, RPI = 32 / S, RP128 = 8 / S;  // slots per row, rows per store, rows per 128 B
+  const int swz = (lane / RP128) & (S - 1);
+#pragma unroll
+  for (int c = 0; c < S; ++c) stage[lane * S + (c ^ swz)] = vals[c];
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < S; ++k) {
+    const int r = k * RPI + lane / S, sl = lane % S;
+    const uint4 x = stage[r * S + (sl ^ ((r / RP128) & (S - 1)))];
+    if (r < nrows) *reinterpret_cast<uint4*>(base + (size_t)r * stride + sl * 16) = x;
+  }
+  __syncwarp();
+}
+
+// 32 floats as 16-byte words: f32, fp16 hi, fp16 lo (x - hi), or srq codes.
+__device__ __forceinline__ void pack_f32(const float* v, uint4 (&o)[8]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    o[c] = make_uint4(__float_as_uint(v[4 * c]), __float_as_uint(v[4 * c + 1]), __float_as_uint(v[4 * c + 2]),
+                      __float_as_uint(v[4 * c + 3]));
+}
+template <bool LO>
+__device__ __forceinline__ void pack_f16(const float* v, uint4* o, int nwords16) {
+#pragma unroll
+  for (int c = 0; c < nwords16; ++c) {
+    uint32_t w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint32_t hw, lw;
+      split2_f16(v[8 * c + 2 * u], v[8 * c + 2 * u + 1], hw, lw);
+      w[u] = LO ? lw : hw;
+    }
+    o[c] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+__device__ __forceinline__ void pack_codes(const float* v, float sc, uint4 (&o)[4]) {
+  const float inv = 1.0f / sc;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint32_t w[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      union {
+        __half2 h;
+        uint32_t x;
+      } cv;
+      cv.h = __floats2half2_rn(srq_code(v[8 * c + 2 * u], sc, inv), srq_code(v[8 * c + 2 * u + 1], sc, inv));
+      w[u] = cv.x;
+    }
+    o[c] = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -245,6 +340,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;
     const int eg = (warp - 2) >> 2;
     const int row_in_tile = 32 * q + lane;
+    uint4* stage = reinterpret_cast<uint4*>(smem + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_STAGE);
     uint32_t t = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
       const uint32_t buf = t & 1, use = t >> 1;
@@ -256,6 +352,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t tb = tmem_base + ((uint32_t)(32 * q) << 16) + buf * BN;
       const int row = mb * BM + row_in_tile;
       const bool valid = row < a.M;
+      const int wrow0 = mb * BM + 32 * q, wrows = a.M - wrow0;  // this warp's 32-row block
       const float rs = a.row_scale;
 
       if (EPI == EPI_F32 || EPI == EPI_PATCH || EPI == EPI_SILU) {
@@ -297,14 +394,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int j = 0; j < 32; ++j) v[j] = v[j] + bs[j];
               }
             }
-            if (EPI == EPI_SILU) {
-              if (a.s_code != 0.0f) store_codes_row(a.out_hi + (size_t)row * a.ldh + n0, v, a.s_code, 32);
-              else store_f16x2_row(a.out_hi + (size_t)row * a.ldh + n0, a.out_lo + (size_t)row * a.ldh + n0, v, 32);
+          }
+          const int n0 = nb * BN + c * 32;
+          if (EPI == EPI_SILU) {
+            char* bh_ = reinterpret_cast<char*>(a.out_hi + (size_t)wrow0 * a.ldh + n0);
+            if (a.s_code != 0.0f) {
+              uint4 w[4];
+              pack_codes(v, a.s_code, w);
+              warp_store_block<64>(stage, w, bh_, (size_t)a.ldh * 2, wrows, lane);
             } else {
-              float* dst = a.out_f32 + (size_t)row * a.ldo + n0;
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              uint4 w[4];
+              pack_f16<false>(v, w, 4);
+              warp_store_block<64>(stage, w, bh_, (size_t)a.ldh * 2, wrows, lane);
+              pack_f16<true>(v, w, 4);
+              warp_store_block<64>(stage, w, reinterpret_cast<char*>(a.out_lo + (size_t)wrow0 * a.ldh + n0),
+                                   (size_t)a.ldh * 2, wrows, lane);
             }
+          } else {
+            uint4 w[8];
+            pack_f32(v, w);
+            warp_store_block<128>(stage, w, reinterpret_cast<char*>(a.out_f32 + (size_t)wrow0 * a.ldo + n0),
+                                  (size_t)a.ldo * 4, wrows, lane);
           }
         }
       } else if (EPI == EPI_GELU_GATE || EPI == EPI_GLU) {
@@ -318,7 +428,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           tmem_ld32(tb + BN / 2 + c * 32, u);
           if (valid) {
             const int ng = nb * BN + c * 32, nu = nb * BN + BN / 2 + c * 32;
-            const int no = nb * (BN / 2) + c * 32;
             float sg[32], su[32];
             load_scales32(a.col_scale + ng, sg);
             load_scales32(a.col_scale + nu, su);
@@ -340,14 +449,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (EPI == EPI_GELU_GATE) g[j] = gelu_tanh_f(g[j]) * u[j];  // runVisionMlpActivationCpu
               else g[j] = g[j] * sigmoid_f(u[j]);                          // runGluActivationCpu
             }
-            if (EPI == EPI_GELU_GATE) {
-              if (a.s_code != 0.0f) store_codes_row(a.out_hi + (size_t)row * a.ldh + no, g, a.s_code, 32);
-              else store_f16x2_row(a.out_hi + (size_t)row * a.ldh + no, a.out_lo + (size_t)row * a.ldh + no, g, 32);
+          }
+          const int no = nb * (BN / 2) + c * 32;
+          if (EPI == EPI_GELU_GATE) {
+            char* bh_ = reinterpret_cast<char*>(a.out_hi + (size_t)wrow0 * a.ldh + no);
+            if (a.s_code != 0.0f) {
+              uint4 w[4];
+              pack_codes(g, a.s_code, w);
+              warp_store_block<64>(stage, w, bh_, (size_t)a.ldh * 2, wrows, lane);
             } else {
-              float* dst = a.out_f32 + (size_t)row * a.ldo + no;
-#pragma unroll
-              for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(dst + j) = make_float4(g[j], g[j + 1], g[j + 2], g[j + 3]);
+              uint4 w[4];
+              pack_f16<false>(g, w, 4);
+              warp_store_block<64>(stage, w, bh_, (size_t)a.ldh * 2, wrows, lane);
+              pack_f16<true>(g, w, 4);
+              warp_store_block<64>(stage, w, reinterpret_cast<char*>(a.out_lo + (size_t)wrow0 * a.ldh + no),
+                                   (size_t)a.ldh * 2, wrows, lane);
             }
+          } else {
+            uint4 w[8];
+            pack_f32(g, w);
+            warp_store_block<128>(stage, w, reinterpret_cast<char*>(a.out_f32 + (size_t)wrow0 * a.ldo + no),
+                                  (size_t)a.ldo * 4, wrows, lane);
           }
         }
       } else if (EPI == EPI_QKV_VISION) {
@@ -362,56 +484,83 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const float so = which == 0 ? a.s_out : (which == 1 ? a.s_out_b : a.s_out_c);
         const float rsw = AMODE == 1 ? (which == 0 ? rs : (which == 1 ? a.row_scale_b : a.row_scale_c)) : rs;
         const float* nw = which == 0 ? a.qn_w : (which == 1 ? a.kn_w : nullptr);
+        if (which < 2) {
+          // the warp's 32 rows are consecutive tokens of one image when the
+          // image's rows are a multiple of 32: then q / k leave as one block
+          const bool block = a.rows_per_image % 32 == 0;
 #pragma unroll 1
-        for (int hh = eg * NH; hh < (eg + 1) * NH; ++hh) {
-          float v[64];
-          tmem_ld32(tb + hh * 64, v);
-          tmem_ld32(tb + hh * 64 + 32, v + 32);
-          if (valid) {
-            const int n0 = n_tile0 + hh * 64;
-            float sc[32];
-            load_scales32(a.col_scale + n0, sc);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = (v[j] * rsw) * sc[j];
-            load_scales32(a.col_scale + n0 + 32, sc);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[32 + j] = (v[32 + j] * rsw) * sc[j];
-            if (so != 0.0f) {
-#pragma unroll
-              for (int j = 0; j < 64; ++j) v[j] = srq_f(v[j], so);
-            }
-            float ss = 0.f;
-#pragma unroll
-            for (int j = 0; j < 64; ++j) ss = fmaf(v[j], v[j], ss);
-            const float inv = 1.0f / sqrtf(ss / 64.0f + a.eps);
-            if (nw) {
-#pragma unroll
-              for (int j = 0; j < 64; ++j) v[j] = (v[j] * inv) * __ldg(nw + j);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 64; ++j) v[j] = v[j] * inv;
-            }
-            const int head = head0 + hh;
-            const size_t bh = (size_t)img * a.heads + head;
-            if (which < 2) {
+          for (int hh = eg * NH; hh < (eg + 1) * NH; ++hh) {
+            float v[64];
+            tmem_ld32(tb + hh * 64, v);
+            tmem_ld32(tb + hh * 64 + 32, v + 32);
+            if (valid) {
+              qkv_head_norm(v, a.col_scale + n_tile0 + hh * 64, rsw, so, a.eps, nw);
               const float4* cs = reinterpret_cast<const float4*>(a.rope_cs) + (size_t)tok * 16;
-              float o[64];
 #pragma unroll
-              for (int p = 0; p < 2; ++p) {
+              for (int p = 0; p < 2; ++p) {  // rotate-half pairs (f, f + 16) in place
 #pragma unroll
                 for (int f = 0; f < 16; f += 2) {
                   const float4 c2 = __ldg(cs + (p * 16 + f) / 2);  // (cos, sin) of f and f + 1
                   const float x1 = v[p * 32 + f], x2 = v[p * 32 + 16 + f];
                   const float y1 = v[p * 32 + f + 1], y2 = v[p * 32 + 16 + f + 1];
-                  o[p * 32 + f] = x1 * c2.x - x2 * c2.y;
-                  o[p * 32 + 16 + f] = x2 * c2.x + x1 * c2.y;
-                  o[p * 32 + f + 1] = y1 * c2.z - y2 * c2.w;
-                  o[p * 32 + 16 + f + 1] = y2 * c2.z + y1 * c2.w;
+                  v[p * 32 + f] = x1 * c2.x - x2 * c2.y;
+                  v[p * 32 + 16 + f] = x2 * c2.x + x1 * c2.y;
+                  v[p * 32 + f + 1] = y1 * c2.z - y2 * c2.w;
+                  v[p * 32 + 16 + f + 1] = y2 * c2.z + y1 * c2.w;
                 }
               }
+            }
+            if (block) {
+              const size_t bh0 = (size_t)(wrow0 / a.rows_per_image) * a.heads + head0 + hh;
+              const size_t r0 = bh0 * a.rows_per_image + wrow0 % a.rows_per_image;
+              uint4 w[8];
+              pack_f16<false>(v, w, 8);
+              warp_store_block<128>(stage, w, reinterpret_cast<char*>((which == 0 ? a.q_hi : a.k_hi) + r0 * 64), 128,
+                                    wrows, lane);
+              pack_f16<true>(v, w, 8);
+              warp_store_block<128>(stage, w, reinterpret_cast<char*>((which == 0 ? a.q_lo : a.k_lo) + r0 * 64), 128,
+                                    wrows, lane);
+            } else if (valid) {
+              const size_t bh = (size_t)img * a.heads + head0 + hh;
               __half* dh = (which == 0 ? a.q_hi : a.k_hi) + (bh * a.rows_per_image + tok) * 64;
               __half* dl = (which == 0 ? a.q_lo : a.k_lo) + (bh * a.rows_per_image + tok) * 64;
-              store_f16x2_row(dh, dl, o, 64);
+              store_f16x2_row(dh, dl, v, 64);
+            }
+          }
+        } else {
+          // V^T: lanes of consecutive tokens pair up (one 32-bit store per
+          // dimension and lane: even lanes the hi plane, odd lanes the lo
+          // plane) when no pair can straddle two images; rows at or past M
+          // then come in whole pairs, and every lane computes so that the
+          // shuffles are full.
+          const bool pair_v = (a.rows_per_image & 1) == 0;
+#pragma unroll 1
+          for (int hh = eg * NH; hh < (eg + 1) * NH; ++hh) {
+            float v[64];
+            tmem_ld32(tb + hh * 64, v);
+            tmem_ld32(tb + hh * 64 + 32, v + 32);
+            if (!valid && !pair_v) continue;
+            qkv_head_norm(v, a.col_scale + n_tile0 + hh * 64, rsw, so, a.eps, nullptr);
+            const size_t bh = (size_t)img * a.heads + head0 + hh;
+            if (pair_v) {
+              const bool odd = lane & 1;  // tok has the parity of the lane (tiles start at even rows)
+              __half* dst = (odd ? a.vt_lo : a.vt_hi) + bh * 64 * (size_t)a.vt_pitch + (tok & ~1);
+#pragma unroll
+              for (int j = 0; j < 64; j += 2) {
+                // hi / lo of dims j and j + 1 as half2 words; even lanes send their lo
+                // word and keep the hi one, odd lanes the reverse
+                uint32_t hw, lw;
+                split2_f16(v[j], v[j + 1], hw, lw);
+                const uint32_t other = __shfl_xor_sync(0xffffffffu, odd ? hw : lw, 1);
+                const uint32_t own = odd ? lw : hw;
+                // (even token, odd token) for dim j, then for dim j + 1
+                const uint32_t w0 = odd ? __byte_perm(other, own, 0x5410) : __byte_perm(own, other, 0x5410);
+                const uint32_t w1 = odd ? __byte_perm(other, own, 0x7632) : __byte_perm(own, other, 0x7632);
+                if (valid) {
+                  *reinterpret_cast<uint32_t*>(dst + (size_t)j * a.vt_pitch) = w0;
+                  *reinterpret_cast<uint32_t*>(dst + (size_t)(j + 1) * a.vt_pitch) = w1;
+                }
+              }
             } else {
               __half* dh = a.vt_hi + bh * 64 * (size_t)a.vt_pitch + tok;
               __half* dl = a.vt_lo + bh * 64 * (size_t)a.vt_pitch + tok;
