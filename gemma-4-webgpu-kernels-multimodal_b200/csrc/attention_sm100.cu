@@ -254,7 +254,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     // softmax of query tile t: one row per thread, TMEM lane quarter (warp % 4)
     const int t = (warp - 2) >> 2;
     const int qw = warp & 3;
-    const int r = 32 * qw + lane;
     const uint32_t lane_base = (uint32_t)(32 * qw) << 16;
     const uint32_t s_col = tmem + lane_base + t * KT;
     const uint32_t o_col = tmem + lane_base + O_COL + t * 2 * HD;
@@ -349,41 +348,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const float inv = 1.0f / l;
       const float inv_code = s_code != 0.0f ? 1.0f / s_code : 0.0f;
-      const int qrow = q0 + t * QT + r;
       const int img = bh / heads, head = bh % heads;
-      const size_t orow = (size_t)img * n + qrow;
-      __half* dh = o_hi + orow * (size_t)(heads * HD) + head * HD;
-      __half* dl = o_lo + orow * (size_t)(heads * HD) + head * HD;
+      // this warp's 32 query rows leave as one block through its 4 KB of the
+      // tile's Q region (free: the tile's last S MMA completed before its
+      // last softmax), whole sectors per store
+      uint4* stage = reinterpret_cast<uint4*>(sm + Q_OFF + 2 * t * TILE_BYTES + qw * 4096);
+      const int wq0 = q0 + t * QT + 32 * qw;  // query row of lane 0
+      const size_t ostride = (size_t)heads * HD * 2;
+      const size_t obase = ((size_t)img * n + wq0) * (size_t)(heads * HD) + head * HD;
+      // one plane at a time (hi, lo or codes), the O columns re-read from
+      // TMEM chunk by chunk so that only the plane's eight words stay live
+      const int planes = s_code != 0.0f ? 1 : 2;
 #pragma unroll 1
-      for (int h = 0; h < HD / 16; ++h) {
-        uint32_t ov[16], ol[16];
-        tmem_ld16_nw(o_col + 16 * h, ov);       // P * Vh
-        tmem_ld16_nw(o_col + HD + 16 * h, ol);  // P * Vl
-        tmem_wait_ld();
-        if (qrow < n) {
+      for (int pl = 0; pl < planes; ++pl) {
+        uint4 w[8];
 #pragma unroll
-          for (int i = 0; i < 16; i += 8) {
-            uint32_t hv[4], lv[4];
+        for (int h = 0; h < HD / 16; ++h) {
+          uint32_t ov[16], ol[16];
+          tmem_ld16_nw(o_col + 16 * h, ov);       // P * Vh
+          tmem_ld16_nw(o_col + HD + 16 * h, ol);  // P * Vl
+          tmem_wait_ld();
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            uint32_t q4[4];
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
-              const int c0 = i + 2 * u, c1 = c0 + 1;
-              const float x0 = (__uint_as_float(ov[c0]) + __uint_as_float(ol[c0])) * inv;
-              const float x1 = (__uint_as_float(ov[c1]) + __uint_as_float(ol[c1])) * inv;
+              const int i = 8 * half + 2 * u;
+              const float x0 = (__uint_as_float(ov[i]) + __uint_as_float(ol[i])) * inv;
+              const float x1 = (__uint_as_float(ov[i + 1]) + __uint_as_float(ol[i + 1])) * inv;
               if (s_code != 0.0f) {  // integer codes for the o_proj input scale
                 union {
                   __half2 h2;
-                  uint32_t w;
+                  uint32_t wd;
                 } cv;
                 cv.h2 = __floats2half2_rn(srq_code(x0, s_code, inv_code), srq_code(x1, s_code, inv_code));
-                hv[u] = cv.w;
+                q4[u] = cv.wd;
               } else {
-                split2_f16(x0, x1, hv[u], lv[u]);
+                uint32_t hw, lw;
+                split2_f16(x0, x1, hw, lw);
+                q4[u] = pl ? lw : hw;
               }
             }
-            *reinterpret_cast<uint4*>(dh + 16 * h + i) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-            if (s_code == 0.0f) *reinterpret_cast<uint4*>(dl + 16 * h + i) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+            w[2 * h + half] = make_uint4(q4[0], q4[1], q4[2], q4[3]);
           }
         }
+        warp_store_block<128>(stage, w, reinterpret_cast<char*>((pl ? o_lo : o_hi) + obase), ostride, n - wq0, lane);
       }
     }
     tc_fence_before();

@@ -110,6 +110,30 @@ constexpr float kLog2eF = 1.4426950408889634f;
 // sigmoid(x) = 1 / (1 + 2^(-x log2 e)); saturates to 0 / 1 without NaN.
 __device__ __forceinline__ float sigmoid_f(float x) { return rcp_approx(1.0f + ex2_approx(-x * kLog2eF)); }
 
+// Warp-cooperative store of a 32-row block: block row r belongs to lane r,
+// whose RB bytes are vals[0 .. RB/16).  The rows pass through the warp's
+// shared-memory stage (16-byte slots XOR-swizzled so that both phases are
+// bank-conflict free) and leave row-contiguously, RB/16 lanes per row, so
+// every store instruction writes whole 32-byte sectors of 512/RB rows rather
+// than a 16-byte piece of each of 32 rows.  Block row r goes to
+// base + r * stride (bytes); rows r >= nrows are not written.
+template <int RB>
+__device__ __forceinline__ void warp_store_block(uint4* stage, const uint4 (&vals)[RB / 16], char* base,
+                                                 size_t stride, int nrows, int lane) {
+  constexpr int S = RB / 16, RPI = 32 / S, RP128 = 8 / S;  // slots per row, rows per store, rows per 128 B
+  const int swz = (lane / RP128) & (S - 1);
+#pragma unroll
+  for (int c = 0; c < S; ++c) stage[lane * S + (c ^ swz)] = vals[c];
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < S; ++k) {
+    const int r = k * RPI + lane / S, sl = lane % S;
+    const uint4 x = stage[r * S + (sl ^ ((r / RP128) & (S - 1)))];
+    if (r < nrows) *reinterpret_cast<uint4*>(base + (size_t)r * stride + sl * 16) = x;
+  }
+  __syncwarp();
+}
+
 // Untiled bulk copy of `bytes` from global memory into this CTA's shared
 // memory, completing on `bar`.  Both addresses 16-byte aligned, bytes a
 // multiple of 16.
