@@ -264,9 +264,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) break;
       tc_fence_after();
       const int kvalid = n - j * KT;  // < KT only on the last tile
-      float mp[8];                    // pass 1: eight independent max chains
+      float mp[8];  // pass 1: eight independent max chains
+      // the whole score row; pass 2 reuses chunks 0 and 1 from here and
+      // reloads chunks 2 and 3 into registers whose values are dead by then
+      uint32_t sr[KT];
       {
-        uint32_t sr[KT];
 #pragma unroll
         for (int c = 0; c < KT / 32; ++c) tmem_ld32_nw(s_col + 32 * c, sr + 32 * c);
         tmem_wait_ld();
@@ -308,18 +310,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (need) m = mt;
         }
       }
-      // pass 2: P = 2^(s log2e - m) chunk by chunk (32 keys), the next chunk's
-      // TMEM load in flight while this one is converted; P hi / lo go back
-      // into the chunk's own columns.
+      // pass 2: P = 2^(s log2e - m) chunk by chunk (32 keys); chunks 0 and 1
+      // come from pass 1's registers, chunks 2 and 3 are reloaded while
+      // chunks 0 and 1 are converted; P hi / lo go back into the chunk's own
+      // columns.
       const float mneg = -m;
       float rp[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
-      uint32_t buf[2][32];
-      tmem_ld32_nw(s_col, buf[0]);
-      tmem_wait_ld();
+      tmem_ld32_nw(s_col + 64, sr + 64);    // chunk 2
 #pragma unroll
       for (int c = 0; c < KT / 32; ++c) {
-        uint32_t* cur = buf[c & 1];
-        if (c + 1 < KT / 32) tmem_ld32_nw(s_col + 32 * (c + 1), buf[(c + 1) & 1]);
+        // chunk c's 32 scores: 0 -> sr[0..32), 1 -> sr[32..64), 2 -> sr[64..96), 3 -> sr[0..32) (reloaded)
+        uint32_t* cur = sr + (c == 1 ? 32 : (c == 2 ? 64 : 0));
+        if (c == 1) tmem_ld32_nw(s_col + 96, sr);  // chunk 3, over chunk 0's dead values
+        if (c == 2) tmem_wait_ld();                // chunks 2 and 3 have landed
         const int lim = kvalid - 32 * c;  // keys of this chunk that are valid (>= 32: all)
         uint32_t hv[16], lv[16];
 #pragma unroll
@@ -335,7 +338,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tmem_st16(s_col + 32 * c, hv);
         tmem_st16(s_col + 32 * c + 16, lv);
-        if (c + 1 < KT / 32) tmem_wait_ld();
       }
       tmem_wait_st();
       tc_fence_before();

@@ -116,24 +116,6 @@ __device__ __forceinline__ void load_scales32(const float* p, float* s) {
   }
 }
 
-// Codes for the next GEMM's input scale (EPI_GELU_GATE / EPI_SILU outputs).
-__device__ __forceinline__ void store_codes_row(__half* dst, const float* v, float s, int n) {
-  const float inv = 1.0f / s;
-  for (int j = 0; j < n; j += 8) {
-    uint32_t hv[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      union {
-        __half2 h;
-        uint32_t w;
-      } c;
-      c.h = __floats2half2_rn(srq_code(v[j + 2 * u], s, inv), srq_code(v[j + 2 * u + 1], s, inv));
-      hv[u] = c.w;
-    }
-    *reinterpret_cast<uint4*>(dst + j) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-  }
-}
-
 // 32 floats as 16-byte words: f32, fp16 hi, fp16 lo (x - hi), or srq codes.
 __device__ __forceinline__ void pack_f32(const float* v, uint4 (&o)[8]) {
 #pragma unroll
