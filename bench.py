@@ -294,6 +294,13 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     dom = max(gem, key=lambda k: gem[k][1])
     peak = measured_peaks().get("bf16_tflops_sustained") or 1400.0
     ach = flops[dom] / (gem[dom][1] / gem[dom][0] / 1000.0) / 1e12
+    traffic = None  # DRAM bytes per launch of the dominant kernel, from an ncu capture
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic_per_launch.json")))
+        if args.clips == 128 and world == 1:
+            traffic = tr.get(dom, {}).get("bytes_per_launch_audio128")
+    except Exception:
+        pass
     # end to end with pinned host clips through the C ABI batch call
     clips = [host[int(offs[i]):int(offs[i]) + int(lens[i])].numpy() for i in range(n)]
     out_pin = torch.empty((rows, 1536), dtype=torch.float32).pin_memory()
@@ -321,7 +328,7 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
         "e2e": {"value": job_seconds * k_e2e / te, "unit": "audio-s/s",
                 "h2d_bytes_per_step": total * 4, "d2h_bytes_per_step": rows * 1536 * 4},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                     "frac": ach / peak, "peak_source": "measured (bf16 cuBLAS, sustained)", "traffic": None,
+                     "frac": ach / peak, "peak_source": "measured (bf16 cuBLAS, sustained)", "traffic": traffic,
                      "launch_ms": gem[dom][1] / gem[dom][0], "flop_per_launch": flops[dom]},
         "kernel_ms_per_step": {k: round(v[1], 4) for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
     }
