@@ -40,7 +40,10 @@ def _oracle_case(oracle, syn, W, h, w, max_soft, layers, seed=0):
     return pix, emb, patches, pos
 
 
-@pytest.mark.parametrize("hw,max_soft,layers", [((96, 96), 4, 2), ((48, 48), 1, 4), ((144, 96), 6, 3)])
+# patch counts: 36 (even), 9 (odd: per-row q | k | v stores), 54, and 288 (a
+# multiple of 32: 32-row block stores, with a last GEMM row tile of 32 rows)
+@pytest.mark.parametrize("hw,max_soft,layers",
+                         [((96, 96), 4, 2), ((48, 48), 1, 4), ((144, 96), 6, 3), ((192, 384), 32, 2)])
 def test_vision_small_stack(vis, oracle, syn, hw, max_soft, layers):
     c, W, _ = vis
     pix, ref, _, _ = _oracle_case(oracle, syn, W, hw[0], hw[1], max_soft, layers)
