@@ -228,8 +228,10 @@ def run_reference(args):
         "unit": "images/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1000.0 * sum(secs) / len(secs), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (JS number / Math.fround semantics)", "data": "synthetic",
-        "config": {"workload": "vision batch, 768x768 images, 16 layers, reference CPU path (bounded sample)",
-                   "image": "768x768", "layers": 16, "activation_quant": QUANT_DESC[args.quant]},
+        # the same workload as the CUDA arm's line; each step times a bounded sample of it (cpu_baseline.sample)
+        "config": {"workload": f"batched vision: {args.batch} images/GPU of 768x768 (2304 patches, 256 tokens), 16 layers",
+                   "images_per_gpu": args.batch, "image": "768x768", "layers": 16,
+                   "parallelism": f"dp{args.gpus} (replicas)", "activation_quant": QUANT_DESC[args.quant]},
         "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
@@ -238,8 +240,13 @@ def run_reference(args):
         a_secs = [cpu_audio_sample(threads, args.quant)[0] for _ in range(max(1, min(args.steps, 3)))]
         av = len(a_secs) / sum(a_secs)
         line["audio"] = {"metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": av,
-                         "unit": "audio-s/s", "cpu_baseline": {"value": av, "unit": "audio-s/s", "cores": threads,
-                                                               "kind": "port", "sample": AUDIO_SAMPLE_DESC}}
+                         "unit": "audio-s/s",
+                         "config": {"workload": f"batched audio: {args.clips} clips/GPU, lengths U[1,30] s (seeded), "
+                                                "packed rows (no padding), clips LPT-balanced over the ranks by encoder rows",
+                                    "clips_per_gpu": args.clips, "activation_quant": QUANT_DESC[args.quant]},
+                         "cpu_baseline": {"value": av, "unit": "audio-s/s", "cores": threads,
+                                          "kind": "port", "sample": AUDIO_SAMPLE_DESC},
+                         "e2e": {"value": av, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
