@@ -23,7 +23,7 @@
 // Ah [Bh | Bl] (N = 64) and Al Bh (N = 32).  The epilogue thread of
 // position (t1, f1) holds its 32 channels, so the LayerNorm is thread-local
 // (double statistics, as the reference's JS numbers).
-//   warp 0  TMA producer (3-stage ring)   warp 1  TMEM owner + MMA issuer
+//   warp 0  TMA producer (2-stage ring; two CTAs per SM)   warp 1  TMEM owner + MMA issuer
 //   warps 2..5  epilogue (warp % 4 = output row of the tile, lane = f1)
 #include "g4m_kernels.h"
 #include "g4m_sm100.cuh"
@@ -34,7 +34,7 @@ namespace {
 constexpr int SA_BYTES = 128 * 128;  // A tile: 128 positions x 64 channels fp16
 constexpr int SB_BYTES = 32 * 128;   // B tile: 32 output channels x 64 channels fp16
 constexpr int SSTAGE = 2 * SA_BYTES + 2 * SB_BYTES;
-constexpr int SSTAGES = 3;
+constexpr int SSTAGES = 2;  // 2 stages: two CTAs per SM, one's epilogue overlapping the other's mainloop
 constexpr int SKB = 18;              // k-blocks: 9 taps x 2 channel halves
 constexpr int SUB_SMEM = SSTAGES * SSTAGE + 1024;
 constexpr int SUB_THREADS = 192;
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restri
   }
 }
 
-__global__ void __launch_bounds__(SUB_THREADS, 1)
+__global__ void __launch_bounds__(SUB_THREADS, 2)
     subsample_conv_tc_kernel(const __grid_constant__ CUtensorMap mLh, const __grid_constant__ CUtensorMap mLl,
                              const __grid_constant__ CUtensorMap mWh, const __grid_constant__ CUtensorMap mWl,
                              const int* __restrict__ t0off, const int* __restrict__ row0, const int* __restrict__ rows,
