@@ -417,25 +417,45 @@ __global__ void __launch_bounds__(128, 4) audio_attn_kernel(const float* __restr
           mma_16816(ox[n], al, bh0, bh1);
         }
       }
+      // The fragments (16 bytes of each of 8 rows per store) go through the
+      // warp's 2 KB of the query region (free until the next block's
+      // install) as [16 rows][64 B] hi and lo planes, 16-byte chunks
+      // XOR-swizzled by row pair, and leave as 64 contiguous bytes per row.
+      uint32_t* sth = reinterpret_cast<uint32_t*>(at_smem + warp * 2048);
+      uint32_t* stl = sth + 256;
 #pragma unroll
       for (int n = 0; n < 4; ++n) {
-        const int dim = head * HD + warp * 32 + n * 8 + 2 * tig;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const int qi = g + 8 * half;
-          if (qi >= nq) continue;
           const float o0 = fmaf(ox[n][2 * half], kLoInv, oh[n][2 * half]);
           const float o1 = fmaf(ox[n][2 * half + 1], kLoInv, oh[n][2 * half + 1]);
-          const long oi = (r0 + b * CH + qi) * D + dim;
+          const int wd = qi * 16 + 4 * (n ^ ((qi >> 1) & 3)) + tig;
           if (s_code != 0.0f) {  // integer codes for the post projection's input scale
-            *reinterpret_cast<__half2*>(o_hi + oi) = __halves2half2(
-                __float2half_rn(srq_code(o0, s_code, inv_code)), __float2half_rn(srq_code(o1, s_code, inv_code)));
+            union {
+              __half2 h2;
+              uint32_t w;
+            } cv;
+            cv.h2 = __halves2half2(__float2half_rn(srq_code(o0, s_code, inv_code)),
+                                   __float2half_rn(srq_code(o1, s_code, inv_code)));
+            sth[wd] = cv.w;
           } else {
             uint32_t hv, lv;
             split2_f16(o0, o1, hv, lv);
-            *reinterpret_cast<uint32_t*>(o_hi + oi) = hv;
-            *reinterpret_cast<uint32_t*>(o_lo + oi) = lv;
+            sth[wd] = hv;
+            stl[wd] = lv;
           }
+        }
+      }
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int qi = 8 * k + (lane >> 2), c = lane & 3;
+        if (qi < nq) {
+          const int wd = qi * 16 + 4 * (c ^ ((qi >> 1) & 3));
+          const long oi = (r0 + b * CH + qi) * D + head * HD + warp * 32 + c * 8;
+          *reinterpret_cast<uint4*>(o_hi + oi) = *reinterpret_cast<const uint4*>(sth + wd);
+          if (s_code == 0.0f) *reinterpret_cast<uint4*>(o_lo + oi) = *reinterpret_cast<const uint4*>(stl + wd);
         }
       }
     }
