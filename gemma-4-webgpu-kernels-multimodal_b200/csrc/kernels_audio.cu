@@ -174,7 +174,9 @@ cudaError_t audio_logmel(const float* samples, const long* sample_off, const lon
 //   softmax  one warp per query row, lane = context slot: tanh softcap, max,
 //            exp, sum; weights of out-of-clip slots kept in the denominator;
 //            P written as hi / lo planes in ring order
-//   P*V      [16 x 32 ring slots] x [32 x 128]: warp w takes dims [32w, +32)
+//   P*V      [16 x 32 ring slots] x [32 x 128]: warp w takes dims [32w, +32);
+//            its output rows pass through a staging block in the (by then
+//            free) query region and leave as 64 contiguous bytes per row
 // qkv: [rows][3 * 1024] f32 (q | k | v); relk: [13][1024]; qmul: [128]
 // (= 128^-0.5 / ln 2 * softplus(per_dim_scale)); kscale = ln(1 + e) / ln 2.
 // ---------------------------------------------------------------------------
