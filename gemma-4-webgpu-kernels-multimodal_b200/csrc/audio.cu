@@ -406,7 +406,7 @@ static void next_scales(RowArgs& r, const float* s, int n, __half* a_c) {
 // Row metadata of a packed batch: clip of every row, first row and row count
 // of every clip, attention runs (clip, first of up to kAudioAttnRun blocks
 // of 12 rows).
-static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out, int* nblocks, cudaStream_t st,
+static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out, int* nruns, cudaStream_t st,
                             HostKeep* keep = nullptr) {
   const int n = (int)rows.size();
   std::vector<int> row0(n);
@@ -441,7 +441,7 @@ static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out
   G4M_LAUNCH_A(upload_meta(b.t1_len.p, bidx.data(), bidx.size() * 4, st, keep));
   if (!keep) G4M_LAUNCH_A(cudaStreamSynchronize(st));  // the host vectors above are the copy sources
   *M_out = M;
-  *nblocks = (int)bclip.size();
+  *nruns = (int)bclip.size();
   return G4M_OK;
 }
 
@@ -449,7 +449,7 @@ static int audio_setup_rows(Device& d, const std::vector<int>& rows, long* M_out
 // holds the residual stream and ab.a_* the feed_forward1 pre-norm operand of
 // layer `first`; on exit ab.h holds the output of the last layer (after
 // norm_out) and, if another layer follows, ab.a_* its first operand.
-static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int first, int count, bool next_operand,
+static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nruns, int first, int count, bool next_operand,
                              cudaStream_t st) {
   AudioWeights& aw = d.aw;
   AudioBuffers& b = d.ab;
@@ -528,7 +528,7 @@ static int audio_layer_range(g4m_ctx* ctx, Device& d, long M, int nblocks, int f
     if (qkv_codes) G4M_RUN("gemm_qkv", gemm_launch(256, 1, EPI_F32, op, a, st, 0, 1));
     else G4M_RUN("gemm_qkv", gemm_launch(256, 2, EPI_F32, op, a, st));
     G4M_RUN("attention", audio_attention_blocks((const float*)b.qkv.p, L.relk, L.pds, (const int*)b.t1_off.p,
-                                                (const int*)b.t1_len.p, nblocks, drow0, drows,
+                                                (const int*)b.t1_len.p, nruns, drow0, drows,
                                                 (float)(log(1.0 + exp(1.0)) / log(2.0)), 50.0f, ah, al, L.sin_post,
                                                 st));
     a = aargs(d, M, D, D);
@@ -623,8 +623,8 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   T0S += 1;            // and one after the last
   T0S += T0S & 1;      // an even row count (the conv's TMA view pairs rows)
   long M = 0;
-  int nblocks = 0;
-  if ((rc = audio_setup_rows(d, rows, &M, &nblocks, st, keep))) return rc;
+  int nruns = 0;
+  if ((rc = audio_setup_rows(d, rows, &M, &nruns, st, keep))) return rc;
   AudioBuffers& b = d.ab;
   if (ensure(b.sample_off, n * 8) || ensure(b.sample_len, n * 8) || ensure(b.frame_off, n * 4) ||
       ensure(b.frames, n * 4) || ensure(b.feats, FR * 128 * 4) || ensure(b.t0_off, n * 4) ||
@@ -671,7 +671,7 @@ int audio_forward(g4m_ctx* ctx, Device& d, const std::vector<ClipShape>& shapes,
   r.a_lo = al;
   r.lda = D;
   G4M_RUN("rows", fused_rows(r, st));
-  if ((rc = audio_layer_range(ctx, d, M, nblocks, 0, layers, false, st))) return rc;
+  if ((rc = audio_layer_range(ctx, d, M, nruns, 0, layers, false, st))) return rc;
   // output projection + bias (src/audio/kernels.ts:380-413), then the embedder
   G4M_RUN("prep_a", prep_a(h, M, D, 0.0f, nullptr, ah, al, st));
   a = aargs(d, M, OUT, D);
@@ -701,8 +701,8 @@ int audio_layers_host(g4m_ctx* ctx, Device& d, const std::vector<int>& rows, int
   if (rc) return rc;
   cudaStream_t st = d.st;
   long M = 0;
-  int nblocks = 0;
-  if ((rc = audio_setup_rows(d, rows, &M, &nblocks, st))) return rc;
+  int nruns = 0;
+  if ((rc = audio_setup_rows(d, rows, &M, &nruns, st))) return rc;
   AudioBuffers& b = d.ab;
   G4M_LAUNCH_A(cudaMemcpyAsync(b.h.p, h, M * D * 4, cudaMemcpyHostToDevice, st));
   RowArgs r;
@@ -717,7 +717,7 @@ int audio_layers_host(g4m_ctx* ctx, Device& d, const std::vector<int>& rows, int
   r.a_lo = (__half*)b.a_lo.p;
   r.lda = D;
   G4M_RUN("rows", fused_rows(r, st));
-  if ((rc = audio_layer_range(ctx, d, M, nblocks, first, count, false, st))) return rc;
+  if ((rc = audio_layer_range(ctx, d, M, nruns, first, count, false, st))) return rc;
   G4M_LAUNCH_A(cudaMemcpyAsync(h, b.h.p, M * D * 4, cudaMemcpyDeviceToHost, st));
   d.last_audio_rows = M;
   return finish(d, st);
