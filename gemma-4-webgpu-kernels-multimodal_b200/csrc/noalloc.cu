@@ -63,6 +63,11 @@ extern "C" int g4m_linear_run_noalloc(g4m_linear* L, const float* x_dev, int row
   hi.n = (size_t)kNoAllocMaxElems * sizeof(__half);
   lo.p = (__half*)base + kNoAllocMaxElems;
   lo.n = hi.n;
+  // The shared operand path grows a buffer that is too small (cudaFree +
+  // cudaMalloc); on these views that would free a static symbol.  Refuse
+  // here, whatever the limit above says, so that branch is never reached.
+  if ((size_t)rows * (size_t)L->in * sizeof(__half) > hi.n)
+    return fail(G4M_E_SHAPE, "g4m_linear_run_noalloc: operand does not fit the static scratch views");
   cudaStream_t st = stream ? (cudaStream_t)stream : cudaStreamLegacy;  // NULL: the default stream
   return qat_linear_device(d, L->w16, L->scale, L->bias, L->w_raw, L->bits, rows, L->in, L->out, L->s_in, L->s_out,
                            x_dev, y_dev, hi, lo, st);

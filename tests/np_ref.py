@@ -228,3 +228,53 @@ def resize_rgb(img, th, tw):
     tmp = np.einsum("ox,yxc->yoc", axis(w, tw), img)
     out = np.einsum("oy,yxc->oxc", axis(h, th), tmp)
     return (np.clip(np.floor(out + 0.5), 0, 255) / 255.0).astype(np.float32)
+
+
+def bf16_to_f64(bits):
+    """BF16 bit patterns (uint16) -> float64."""
+    b = np.asarray(bits).astype(np.uint32) << 16
+    return b.view(np.float32).astype(np.float64)
+
+
+def vision_layer(W, i, h, pos):
+    """One vision encoder layer in float64 (src/vision/encoder.ts:189-298
+    dataflow: input norm, q / k / v with head norms and 2-D RoPE, attention
+    with scale 1, o_proj, post-attention norm + residual, pre-feedforward
+    norm, gelu-gate MLP, post-feedforward norm + residual)."""
+    p = f"model.vision_tower.encoder.layers.{i}"
+    heads, hd = 12, 64
+
+    def lin(name, x):
+        pre = f"{p}.{name}.linear"
+        return qat_i8(x, W[f"{pre}.weight"], W[f"{pre}.weight_scale"], float(W[f"{pre}.input_activation_scale"]),
+                      float(W[f"{pre}.output_activation_scale"]))
+
+    nw = lambda n: bf16_to_f64(W[f"{p}.{n}.weight"])
+    h = np.asarray(h, np.float64)
+    a = rmsnorm(h, nw("input_layernorm"))
+    q = rmsnorm(lin("self_attn.q_proj", a).reshape(-1, hd), nw("self_attn.q_norm")).reshape(-1, heads * hd)
+    k = rmsnorm(lin("self_attn.k_proj", a).reshape(-1, hd), nw("self_attn.k_norm")).reshape(-1, heads * hd)
+    v = rmsnorm(lin("self_attn.v_proj", a).reshape(-1, hd), np.ones(hd)).reshape(-1, heads * hd)
+    q, k = rope(q, pos, heads, hd), rope(k, pos, heads, hd)
+    o = lin("self_attn.o_proj", attention(q, k, v, heads, hd))
+    h1 = h + rmsnorm(o, nw("post_attention_layernorm"))
+    f = rmsnorm(h1, nw("pre_feedforward_layernorm"))
+    m = gelu_gate(lin("mlp.gate_proj", f), lin("mlp.up_proj", f))
+    return h1 + rmsnorm(lin("mlp.down_proj", m), nw("post_feedforward_layernorm"))
+
+
+def vision_patch_embeddings(W, patches, pos):
+    t = W["model.vision_tower.patch_embedder.position_embedding_table"]
+    return patch_embed(patches, bf16_to_f64(W["model.vision_tower.patch_embedder.input_proj.weight"]), pos,
+                       bf16_to_f64(t[0]), bf16_to_f64(t[1]))
+
+
+def vision_embed(W, patches, pos, grid_h, grid_w, layer_count=16, hidden_out=None):
+    """Vision tower in float64: patch embedding, layers, 3x3 pooler,
+    embedder (src/vision/index.ts:69-112)."""
+    h = vision_patch_embeddings(W, patches, pos)
+    for i in range(layer_count):
+        h = vision_layer(W, i, h, pos)
+        if hidden_out is not None:
+            hidden_out.append(h)
+    return embedder(pooler(h, grid_h, grid_w), W["model.embed_vision.embedding_projection.weight"])

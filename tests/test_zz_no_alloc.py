@@ -69,3 +69,45 @@ def test_noalloc_rejects_past_scratch(ctx, native, syn):
         assert rc == 0 and np.allclose(y, inp * 0.01)
     finally:
         L.g4m_linear_free(h)
+
+
+def test_noalloc_allocates_nothing(ctx, native):
+    """The point of the entry point: a call takes no device memory.  Free
+    device memory is read before and after two calls at the largest row count
+    on a freshly prepared linear (after one warm-up call, which looks up the
+    scratch address).  The same measurement around a first g4m_linear_run on
+    another fresh linear shows the drop that an allocating call causes."""
+    import torch
+    L = native.lib()
+    inp, out = 1024, 256
+    rows = MAX_ELEMS // inp
+    rng = np.random.default_rng(11)
+    w = rng.integers(-127, 128, (out, inp)).astype(np.int8)
+    s = np.full(out, 0.01, np.float32)
+    xd = torch.from_numpy(rng.standard_normal((rows, inp)).astype(np.float32)).cuda()
+    yd = torch.empty((rows, out), dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    handles = []
+    try:
+        for _ in range(2):
+            h = ctypes.c_void_p()
+            native.check(L.g4m_linear_prepare(ctx.h, 0, native.ptr(w), 0, out, inp, native.ptr(s), 0.0, 0.0, None,
+                                              ctypes.byref(h)))
+            handles.append(h)
+        call = lambda fn, h: getattr(L, fn)(h, ctypes.c_void_p(xd.data_ptr()), rows, ctypes.c_void_p(yd.data_ptr()),
+                                            ctypes.c_void_p(st))
+        assert call("g4m_linear_run_noalloc", handles[0]) == 0, native.last_error()
+        torch.cuda.synchronize()
+        free0 = torch.cuda.mem_get_info()[0]
+        for _ in range(2):
+            assert call("g4m_linear_run_noalloc", handles[0]) == 0, native.last_error()
+        torch.cuda.synchronize()
+        free1 = torch.cuda.mem_get_info()[0]
+        assert free1 == free0, f"noalloc calls changed free device memory by {free0 - free1} bytes"
+        assert call("g4m_linear_run", handles[1]) == 0, native.last_error()
+        torch.cuda.synchronize()
+        free2 = torch.cuda.mem_get_info()[0]
+        assert free1 - free2 >= 2 * rows * inp * 2, "the free-memory probe did not see an allocating call"
+    finally:
+        for h in handles:
+            L.g4m_linear_free(h)
