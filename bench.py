@@ -1,23 +1,27 @@
 #!/usr/bin/env python
-"""Benchmark: Gemma 4 E2B vision tower throughput (images/s) on B200.
+"""Benchmark: Gemma 4 E2B vision and audio tower throughput on B200.
 
-Step = one pass of the vision tower (patch embed, 16 encoder layers, 3x3
-pooler, embedder) over a batch of 64 seeded 768x768 images per GPU (the
-batched-vision configuration; weak scaling, one process per GPU under
-torchrun, no data-path collective).  Weights are random-init with the
-reference's dtypes (int8 QAT linears, BF16 norms / patch projection, F32
-embedder); inputs are U[0,1] pixels.
+Default workload (the batched configurations of the benchmark spec):
+- vision: a job of 64 seeded 768x768 images (2304 patches, 256 tokens, all
+  16 layers, pooler, embedder), sharded by image across the N ranks;
+- audio: a job of 128 seeded clips, lengths U[1,30] s, LPT-balanced across
+  the ranks by encoder rows.
+The job is fixed as N grows ("strong" scaling); `--scaling weak` makes
+--images / --clips per-GPU counts instead.  One process per GPU under
+torchrun, no data-path collective (items are independent).
 
-`value` is device-timed (CUDA events on the launching stream, inputs resident
-in HBM, max over ranks); `e2e` is the same metric through the C ABI with
-pinned host buffers (host->device pixels and device->host embeddings inside
-the timed region).  `--impl reference` times the CPU restatement of the
-reference's CPU path (the oracle) on a bounded sample instead.
+A step is one pass of the tower over this rank's share of the job.  `value`
+is device-timed: CUDA events on the launching stream around every timed
+step, inputs resident in HBM, L2 flushed (a 256 MB write) before each step
+outside the events, max over ranks.  `e2e` is the same metric through the
+C ABI batch call with pinned host buffers (host->device inputs and
+device->host embeddings inside the timed region).  `--impl reference` times
+the CPU restatement of the reference's CPU path (the oracle) instead, one
+encoder layer of a full image (or clip) per step.
 """
 from __future__ import annotations
 
 import argparse
-import ctypes
 import importlib
 import json
 import os
@@ -32,6 +36,10 @@ sys.path.insert(0, ROOT)
 PKG = "gemma-4-webgpu-kernels-multimodal_b200"
 
 HIDDEN, FF, HEADS, HD, TEXT = 768, 3072, 12, 64, 1536
+AUDIO_D, AUDIO_FF, AUDIO_OUT = 1024, 4096, 1536
+VISION_METRIC = "images/s (vision tower 768x768, 16 layers, + embedder)"
+AUDIO_METRIC = "audio-sec/s (audio tower, 12 layers, + embedder)"
+FLUSH_BYTES = 256 << 20
 sharding = None  # the package's sharding module, imported with the package
 
 
@@ -50,6 +58,35 @@ def s_in_mode(quant: str):
 
 QUANT_DESC = {"none": "none (input_activation_scale 0: fp16 hi/lo activations, two-term GEMMs)",
               "calibrated": "calibrated (input_activation_scale = absmax/127 per linear: int8 codes, one-term GEMMs)"}
+
+
+def job_images(args, world: int) -> int:
+    return args.images if args.scaling == "strong" else args.images * world
+
+
+def job_clips(args, world: int) -> int:
+    return args.clips if args.scaling == "strong" else args.clips * world
+
+
+def vision_config(args, world: int) -> dict:
+    """The workload both arms report (one definition, so the lines match)."""
+    n = job_images(args, world)
+    per = (f"{n} images in the job, sharded by image over the ranks" if args.scaling == "strong"
+           else f"{args.images} images per GPU")
+    return {"workload": f"batched vision: {per}; 768x768 (2304 patches, 256 tokens), 16 layers + pooler + embedder",
+            "job_images": n, "image": "768x768", "layers": 16, "parallelism": f"dp{world} (replicas)",
+            "l2": "L2 flushed (256 MB write) before every timed step, outside the timed events",
+            "activation_quant": QUANT_DESC[args.quant]}
+
+
+def audio_config(args, world: int) -> dict:
+    n = job_clips(args, world)
+    per = (f"{n} clips in the job" if args.scaling == "strong" else f"{args.clips} clips per GPU")
+    return {"workload": f"batched audio: {per}, lengths U[1,30] s (seeded), packed rows (no padding), clips "
+                        "LPT-balanced over the ranks by encoder rows; 12 layers + output projection + embedder",
+            "job_clips": n, "layers": 12, "parallelism": f"dp{world} (replicas)",
+            "l2": "L2 flushed (256 MB write) before every timed step, outside the timed events",
+            "activation_quant": QUANT_DESC[args.quant]}
 
 
 def weights_path(tower: str, layers: int, quant: str, rank: int, barrier) -> str:
@@ -121,6 +158,21 @@ def measured_peaks():
         return {}
 
 
+def tensor_peak():
+    """(peak TFLOP/s, source): the measured sustained bf16 figure (kernels
+    timed inside seconds-long steps), else the recipe's fallback."""
+    p = measured_peaks().get("bf16_tflops_sustained")
+    return (float(p), "measured (bf16 cuBLAS, sustained)") if p else (1400.0, "fallback")
+
+
+def traffic_per_launch(kernel: str, key: str):
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic_per_launch.json")))
+        return tr.get(kernel, {}).get(key)
+    except Exception:
+        return None
+
+
 def vision_kernel_flops(B: int, N: int, tokens: int):
     """Algorithmic FLOPs per launch of each profiled kernel (2*M*N*K for a
     linear, 4*n^2*d per head for attention), counted once (not per split
@@ -135,33 +187,6 @@ def vision_kernel_flops(B: int, N: int, tokens: int):
         "gemm_patch": 2.0 * M * HIDDEN * 768,
         "gemm_embed": 2.0 * B * tokens * TEXT * HIDDEN,
     }
-
-
-def cpu_vision_sample(threads: int, quant: str = "none"):
-    """Oracle (CPU restatement of the reference's CPU twins) on one 768x768
-    image: patch embedding + one encoder layer + pooler/embedder, scaled to
-    16 layers.  Returns (seconds per image, description)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    syn = importlib.import_module(PKG + ".synthetic")
-    O.set_threads(threads)
-    W = syn.vision_weights(0, layers=1, s_in=s_in_mode(quant))
-    pix = syn.image_pixels(0, 768, 768)
-    pre = O.preprocess_image_pixels(pix)
-    patches, pos = O.valid_image_patch_input(pre)
-    t0 = time.perf_counter()
-    h = O.vision_patch_embeddings(W, patches, pos)
-    t1 = time.perf_counter()
-    h = O.vision_layer(W, 0, h, pos)
-    t2 = time.perf_counter()
-    pooled = O.vision_pooler(h, pos, 256)
-    O.embedder(pooled, W["model.embed_vision.embedding_projection.weight"])
-    t3 = time.perf_counter()
-    per_image = (t1 - t0) + 16 * (t2 - t1) + (t3 - t2)
-    return per_image, "1 image 768x768: patch embed + 1 of 16 encoder layers (x16) + pooler/embedder"
-
-
-AUDIO_D, AUDIO_FF, AUDIO_OUT = 1024, 4096, 1536
 
 
 def audio_kernel_flops(M: int):
@@ -180,93 +205,156 @@ def audio_kernel_flops(M: int):
 
 
 def audio_rows(n: int) -> int:
-    f = (160 + n - 321) // 160 + 1 if 160 + n >= 321 else 0
-    t0 = (f - 1) // 2 + 1 if f else 0
-    return (t0 - 1) // 2 + 1 if f else 0
+    return sharding.encoder_rows(n)
 
 
-AUDIO_SAMPLE_DESC = "one 10 s clip (250 rows): log-mel + subsample + 1 of 12 conformer layers (x12) + output/embedder"
+# ------------------------------------------------------------ CPU (oracle)
 
 
-def cpu_audio_sample(threads: int, quant: str = "none"):
-    """Oracle on one 10 s clip (cfg2): log-mel + subsample + one of 12
-    conformer layers (x12) + output projection / embedder.  Returns (seconds
-    of compute per second of audio, description)."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    syn = importlib.import_module(PKG + ".synthetic")
-    O.set_threads(threads)
-    W = syn.audio_weights(0, layers=1, s_in=s_in_mode(quant))
-    x = syn.audio_samples(0, 160000)
-    t0 = time.perf_counter()
-    pre = O.preprocess_audio(x, pad_to_multiple_of=None)
-    h, mask = O.audio_subsample(W, pre["inputFeatures"], pre["inputFeaturesMask"])
-    t1 = time.perf_counter()
-    h = O.audio_layer(W, 0, h)
-    t2 = time.perf_counter()
-    proj = O.add_bias_rows(O.f32_linear_rows(h, W["model.audio_tower.output_proj.weight"]), W["model.audio_tower.output_proj.bias"])
-    O.embedder(proj, W["model.embed_audio.embedding_projection.weight"])
-    t3 = time.perf_counter()
-    secs = (t1 - t0) + 12 * (t2 - t1) + (t3 - t2)
-    return secs / 10.0, AUDIO_SAMPLE_DESC
+class CpuVisionSteps:
+    """The oracle (CPU restatement of the reference's CPU twins) on one
+    768x768 image, one encoder layer per step: the patch embedding runs with
+    layer 0 and the pooler / embedder with layer 15, so 16 consecutive steps
+    are exactly one image through the whole tower."""
+    DESC = ("one 768x768 image through the oracle, one of the 16 encoder layers per step (patch embedding with "
+            "layer 0, pooler + embedder with layer 15; 16 steps = one image)")
+
+    def __init__(self, threads: int, quant: str):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        syn = importlib.import_module(PKG + ".synthetic")
+        O.set_threads(threads)
+        self.O = O
+        self.W = syn.vision_weights(0, layers=16, s_in=s_in_mode(quant))
+        pre = O.preprocess_image_pixels(syn.image_pixels(0, 768, 768))
+        self.patches, self.pos = O.valid_image_patch_input(pre)
+        self.i = 0
+        self.h = None
+
+    def step(self) -> float:
+        O, layer = self.O, self.i % 16
+        t0 = time.perf_counter()
+        if layer == 0:
+            self.h = O.vision_patch_embeddings(self.W, self.patches, self.pos)
+        self.h = O.vision_layer(self.W, layer, self.h, self.pos)
+        if layer == 15:
+            O.embedder(O.vision_pooler(self.h, self.pos, 256), self.W["model.embed_vision.embedding_projection.weight"])
+        self.i += 1
+        return time.perf_counter() - t0
+
+
+class CpuAudioSteps:
+    """The oracle on one 10 s clip (250 encoder rows), one conformer layer per
+    step: log-mel and subsample run with layer 0, the output projection and
+    embedder with layer 11, so 12 consecutive steps are one clip."""
+    DESC = ("one 10 s clip through the oracle, one of the 12 conformer layers per step (log-mel + subsample with "
+            "layer 0, output projection + embedder with layer 11; 12 steps = one clip)")
+    SECONDS = 10.0
+
+    def __init__(self, threads: int, quant: str):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        syn = importlib.import_module(PKG + ".synthetic")
+        O.set_threads(threads)
+        self.O = O
+        self.W = syn.audio_weights(0, layers=12, s_in=s_in_mode(quant))
+        self.x = syn.audio_samples(0, 160000)
+        self.i = 0
+        self.h = None
+
+    def step(self) -> float:
+        O, W, layer = self.O, self.W, self.i % 12
+        t0 = time.perf_counter()
+        if layer == 0:
+            pre = O.preprocess_audio(self.x, pad_to_multiple_of=None)
+            self.h, _ = O.audio_subsample(W, pre["inputFeatures"], pre["inputFeaturesMask"])
+        self.h = O.audio_layer(W, layer, self.h)
+        if layer == 11:
+            proj = O.add_bias_rows(O.f32_linear_rows(self.h, W["model.audio_tower.output_proj.weight"]),
+                                   W["model.audio_tower.output_proj.bias"])
+            O.embedder(proj, W["model.embed_audio.embedding_projection.weight"])
+        self.i += 1
+        return time.perf_counter() - t0
+
+
+def cpu_rate(make, steps: int, units_per_cycle: float, cycle: int):
+    """Run `steps` oracle steps; rate = units processed / seconds, where a
+    cycle of `cycle` steps processes `units_per_cycle` units."""
+    runner = make()
+    secs = [runner.step() for _ in range(steps)]
+    return units_per_cycle * steps / cycle / sum(secs), secs, runner.DESC
 
 
 def run_reference(args):
-    rank = env_int("RANK", 0)
+    rank, world = env_int("RANK", 0), env_int("WORLD_SIZE", 1)
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    secs = []
-    desc = ""
-    for i in range(args.warmup + args.steps):
-        s, desc = cpu_vision_sample(threads, args.quant)
-        if i >= args.warmup:
-            secs.append(s)
-    value = len(secs) / sum(secs)
+    v = CpuVisionSteps(threads, args.quant)
+    for _ in range(args.warmup):
+        v.step()
+    secs = [v.step() for _ in range(args.steps)]
+    value = (args.steps / 16.0) / sum(secs)
     line = {
-        "impl": "reference", "metric": "images/s (vision tower 768x768, 16 layers, + embedder)", "value": value,
-        "unit": "images/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000.0 * sum(secs) / len(secs), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32 (JS number / Math.fround semantics)", "data": "synthetic",
-        # the same workload as the CUDA arm's line; each step times a bounded sample of it (cpu_baseline.sample)
-        "config": {"workload": f"batched vision: {args.batch} images/GPU of 768x768 (2304 patches, 256 tokens), 16 layers",
-                   "images_per_gpu": args.batch, "image": "768x768", "layers": 16,
-                   "parallelism": f"dp{args.gpus} (replicas)", "activation_quant": QUANT_DESC[args.quant]},
-        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc},
+        "impl": "reference", "metric": VISION_METRIC, "value": value, "unit": "images/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(secs) / len(secs),
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+        "dtype": "f32 (JS number / Math.fround semantics)", "data": "synthetic",
+        "config": vision_config(args, world),
+        "cpu_baseline": {"value": value, "unit": "images/s", "cores": threads, "kind": "port", "sample": v.DESC},
         "e2e": {"value": value, "unit": "images/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
     if not args.no_audio:
-        a_secs = [cpu_audio_sample(threads, args.quant)[0] for _ in range(max(1, min(args.steps, 3)))]
-        av = len(a_secs) / sum(a_secs)
-        line["audio"] = {"metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": av,
-                         "unit": "audio-s/s",
-                         "config": {"workload": f"batched audio: {args.clips} clips/GPU, lengths U[1,30] s (seeded), "
-                                                "packed rows (no padding), clips LPT-balanced over the ranks by encoder rows",
-                                    "clips_per_gpu": args.clips, "activation_quant": QUANT_DESC[args.quant]},
-                         "cpu_baseline": {"value": av, "unit": "audio-s/s", "cores": threads,
-                                          "kind": "port", "sample": AUDIO_SAMPLE_DESC},
+        a = CpuAudioSteps(threads, args.quant)
+        a.step()
+        k = max(args.steps, 12)
+        a_secs = [a.step() for _ in range(k)]
+        av = CpuAudioSteps.SECONDS * (k / 12.0) / sum(a_secs)
+        line["audio"] = {"metric": AUDIO_METRIC, "value": av, "unit": "audio-s/s",
+                         "ms_per_step": 1000.0 * sum(a_secs) / k, "config": audio_config(args, world),
+                         "cpu_baseline": {"value": av, "unit": "audio-s/s", "cores": threads, "kind": "port",
+                                          "sample": a.DESC},
                          "e2e": {"value": av, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
-    """Batched audio (cfg4): 128 clips per GPU, lengths U[1, 30] s, packed
-    without padding rows.  Returns the sub-object of the JSON line (rank 0)."""
+# ----------------------------------------------------------- device arm
+
+
+def timed_steps(step, stream, steps: int, flush):
+    """Device time of `steps` calls of step(): each call bracketed by its own
+    CUDA events on `stream`; the L2 flush before it runs outside them."""
+    import torch
+    evs = []
+    for _ in range(steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def run_audio(args, native, syn, rank, world, dist, barrier, flush):
+    """Batched audio: the job's clips, lengths U[1, 30] s, packed without
+    padding rows, this rank's LPT share.  Returns the sub-object of the JSON
+    line (rank 0)."""
     import numpy as np
     import torch
     p = weights_path("audio", 12, args.quant, rank, barrier)
-    ctx = ctx_cls([torch.cuda.current_device()])
+    ctx = native.Context([torch.cuda.current_device()])
     ctx.load_weights(p)
-    # the job's world * clips clips (one seeded draw), balanced over the ranks
-    # by encoder rows with the batch call's LPT rule
-    job_lens = syn.audio_batch_lengths(1000, world * args.clips)
+    job_lens = syn.audio_batch_lengths(1000, job_clips(args, world))
     mine = sorted(sharding.lpt_assign([audio_rows(int(L)) for L in job_lens], world)[rank])
     lens = job_lens[mine]
     n = len(mine)
     job_seconds = float(job_lens.sum()) / 16000.0
     total = int(lens.sum())
-    host = torch.empty(total, dtype=torch.float32).pin_memory()
+    host = torch.empty(max(total, 1), dtype=torch.float32).pin_memory()
     offs = np.zeros(n, np.int64)
     o = 0
     for j, (i, L) in enumerate(zip(mine, lens)):
@@ -275,23 +363,17 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
         o += int(L)
     dev = host.cuda()
     rows = sum(audio_rows(int(L)) for L in lens)
-    out = torch.empty((rows, 1536), dtype=torch.float32, device="cuda")
+    out = torch.empty((max(rows, 1), 1536), dtype=torch.float32, device="cuda")
     stream = torch.cuda.Stream()
     step = lambda: ctx.audio_embed_device(dev.data_ptr(), offs, lens, out.data_ptr(), stream=stream.cuda_stream)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches0 = native.kernel_launches()
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    e1.synchronize()
+    ms = timed_steps(step, stream, args.steps, flush)
     launches = native.kernel_launches() - launches0
-    ms = sharding.max_over_ranks(e0.elapsed_time(e1), dist, "cuda")
-    audio_seconds = float(lens.sum()) / 16000.0
+    ms = sharding.max_over_ranks(ms, dist, "cuda")
     value = job_seconds * args.steps / (ms / 1000.0)
     ctx.profile_begin()
     step()
@@ -299,18 +381,12 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
     flops = audio_kernel_flops(rows)
     gem = {k: v for k, v in prof.items() if k in flops}
     dom = max(gem, key=lambda k: gem[k][1])
-    peak = measured_peaks().get("bf16_tflops_sustained") or 1400.0
+    peak, peak_src = tensor_peak()
     ach = flops[dom] / (gem[dom][1] / gem[dom][0] / 1000.0) / 1e12
-    traffic = None  # DRAM bytes per launch of the dominant kernel, from an ncu capture
-    try:
-        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic_per_launch.json")))
-        if args.clips == 128 and world == 1:
-            traffic = tr.get(dom, {}).get("bytes_per_launch_audio128")
-    except Exception:
-        pass
+    traffic = traffic_per_launch(dom, "bytes_per_launch_audio128") if n == 128 else None
     # end to end with pinned host clips through the C ABI batch call
     clips = [host[int(offs[i]):int(offs[i]) + int(lens[i])].numpy() for i in range(n)]
-    out_pin = torch.empty((rows, 1536), dtype=torch.float32).pin_memory()
+    out_pin = torch.empty((max(rows, 1), 1536), dtype=torch.float32).pin_memory()
     outs, r0 = [], 0
     for L in lens:
         r = audio_rows(int(L))
@@ -324,34 +400,30 @@ def run_audio(args, ctx_cls, native, syn, rank, world, dist, barrier):
         ctx.audio_embed(clips, 16000, 12, outs=outs)
     te = sharding.max_over_ranks(time.perf_counter() - t0, dist, "cuda")
     res = {
-        "metric": "audio-sec/s (audio tower, 12 layers, + embedder)", "value": value, "unit": "audio-s/s",
-        "ms_per_step": ms / args.steps,
-        "config": {"workload": f"batched audio: {args.clips} clips/GPU, lengths U[1,30] s (seeded), packed rows "
-                               "(no padding), clips LPT-balanced over the ranks by encoder rows",
-                   "clips_per_gpu": args.clips, "clips_this_rank": n, "audio_seconds_job": job_seconds,
-                   "audio_seconds_this_rank": audio_seconds, "encoder_rows_this_rank": rows,
-                   "activation_quant": QUANT_DESC[args.quant]},
+        "metric": AUDIO_METRIC, "value": value, "unit": "audio-s/s", "ms_per_step": ms / args.steps,
+        "config": dict(audio_config(args, world), clips_this_rank=n, audio_seconds_job=job_seconds,
+                       audio_seconds_this_rank=total / 16000.0, encoder_rows_this_rank=rows),
         "gpu_launches": launches,
         "e2e": {"value": job_seconds * k_e2e / te, "unit": "audio-s/s",
                 "h2d_bytes_per_step": total * 4, "d2h_bytes_per_step": rows * 1536 * 4},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                     "frac": ach / peak, "peak_source": "measured (bf16 cuBLAS, sustained)", "traffic": traffic,
+                     "frac": ach / peak, "peak_source": peak_src, "traffic": traffic,
                      "launch_ms": gem[dom][1] / gem[dom][0], "flop_per_launch": flops[dom]},
         "kernel_ms_per_step": {k: round(v[1], 4) for k, v in sorted(prof.items(), key=lambda kv: -kv[1][1])},
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        spa, desc = cpu_audio_sample(os.cpu_count() or 1, args.quant)
-        res["cpu_baseline"] = {"value": 1.0 / spa, "unit": "audio-s/s", "cores": os.cpu_count() or 1, "kind": "port",
-                               "sample": desc}
+        threads = os.cpu_count() or 1
+        rate, _, desc = cpu_rate(lambda: CpuAudioSteps(threads, args.quant), 12, CpuAudioSteps.SECONDS, 12)
+        res["cpu_baseline"] = {"value": rate, "unit": "audio-s/s", "cores": threads, "kind": "port", "sample": desc}
     ctx.close()
     return res
 
 
 def qat_sweep(native, syn, peak, steps=10):
-    """The cfg0 int8 QAT linear (768 -> 768, per-channel scales, bias) on
-    device-resident activations at M = 256 (cfg0 itself), 18432 (8 images)
-    and 147456 (64 images): per-launch CUDA-event time of the tensor-core
-    GEMM, algorithmic TFLOP/s and the fraction of the measured peak."""
+    """The int8 QAT linear (768 -> 768, per-channel scales, bias) on
+    device-resident activations at M = 256, 18432 (8 images) and 147456
+    (64 images): per-launch CUDA-event time of the tensor-core GEMM,
+    algorithmic TFLOP/s and the fraction of the measured peak."""
     import ctypes
     import torch
     L = native.lib()
@@ -389,6 +461,73 @@ def qat_sweep(native, syn, peak, steps=10):
             "peak": peak, "by_rows": out}
 
 
+def qat_cfg0(native, syn, steps=20):
+    """The single int8 QAT linear of the benchmark spec (x f32 [256, 768]
+    ~N(0,1), W int8 [768, 768] U[-127, 127], per-channel scales, bias, seed
+    0): latency through g4m_qat_linear with host buffers (weights uploaded
+    and converted inside the call, as the reference's one-shot runner takes
+    them), the resident form (g4m_linear_run on device buffers, CUDA events),
+    and the oracle on the host's cores.  Parity against the oracle is
+    reported beside the times."""
+    import ctypes
+
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    x, w, s, b = syn.qat_linear_case(0)
+    ctx = native.Context([torch.cuda.current_device()])
+    try:
+        for _ in range(3):
+            y = ctx.qat_linear(x, w, s, bias=b)
+        lat = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            y = ctx.qat_linear(x, w, s, bias=b)
+            lat.append(time.perf_counter() - t0)
+        L = native.lib()
+        h = ctypes.c_void_p()
+        native.check(L.g4m_linear_prepare(ctx.h, 0, native.ptr(w), 0, 768, 768, native.ptr(s), 0.0, 0.0,
+                                          native.ptr(b), ctypes.byref(h)))
+        try:
+            xd = torch.from_numpy(x).cuda()
+            yd = torch.empty((256, 768), dtype=torch.float32, device="cuda")
+            st = torch.cuda.current_stream()
+            run = lambda: native.check(L.g4m_linear_run(h, ctypes.c_void_p(xd.data_ptr()), 256,
+                                                        ctypes.c_void_p(yd.data_ptr()), ctypes.c_void_p(st.cuda_stream)))
+            for _ in range(3):
+                run()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(steps):
+                run()
+            e1.record(st)
+            e1.synchronize()
+            resident_ms = e0.elapsed_time(e1) / steps
+        finally:
+            L.g4m_linear_free(h)
+    finally:
+        ctx.close()
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    cpu = []
+    for _ in range(5):
+        t0 = time.perf_counter()
+        ref = O.add_bias_rows(O.qat_i8_linear(x, w, s), b)
+        cpu.append(time.perf_counter() - t0)
+    rms = float(np.sqrt((ref.astype(np.float64) ** 2).mean()))
+    cos = ((ref * y).sum(1) / (np.linalg.norm(ref, axis=1) * np.linalg.norm(y, axis=1))).min()
+    return {"workload": "int8 QAT linear 256x768 -> 768 + bias, seed 0 (x ~N(0,1), W U[-127,127])",
+            "flop": 2.0 * 256 * 768 * 768,
+            "e2e_ms": round(1000 * statistics.median(lat), 4),
+            "e2e_note": "g4m_qat_linear: host x / W / scales / bias in, host y out; weight upload and fp16 "
+                        "conversion inside every call (the reference's runner takes its weights per call)",
+            "resident_ms": round(resident_ms, 5),
+            "resident_note": "g4m_linear_run: weights prepared once, device x / y, CUDA events",
+            "cpu_ms": round(1000 * statistics.median(cpu), 4), "cpu_cores": threads, "cpu_kind": "port",
+            "max_abs_over_rms": float(np.abs(y - ref).max() / rms), "min_row_cos": float(cos)}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -410,17 +549,21 @@ def run_ours(args):
     syn = importlib.import_module(PKG + ".synthetic")
     global sharding
     sharding = importlib.import_module(PKG + ".sharding")
-    B, H, Wd, layers, max_soft = args.batch, 768, 768, 16, 280
+    H, Wd, layers, max_soft = 768, 768, 16, 280
     N, tokens = (H // 16) * (Wd // 16), 256
+    n_job = job_images(args, world)
+    mine = list(sharding.image_shard(n_job, world, rank))
+    B = len(mine)
     path = weights_path("vision", layers, args.quant, rank, barrier)
     ctx = native.Context([local])
     ctx.load_weights(path)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device="cuda")
 
-    pix_host = torch.empty((B, H, Wd, 3), dtype=torch.float32).pin_memory()
-    for i, seed in enumerate(sharding.image_shard(world * B, world, rank)):  # this rank's images of the job
+    pix_host = torch.empty((max(B, 1), H, Wd, 3), dtype=torch.float32).pin_memory()
+    for i, seed in enumerate(mine):  # this rank's images of the job
         pix_host[i] = torch.from_numpy(syn.image_pixels(seed, H, Wd))
     pix = pix_host.cuda()
-    out = torch.empty((B * tokens, TEXT), dtype=torch.float32, device="cuda")
+    out = torch.empty((max(B, 1) * tokens, TEXT), dtype=torch.float32, device="cuda")
     stream = torch.cuda.Stream()  # a real stream: the library launches on it, the events bracket it
 
     def step():
@@ -434,19 +577,12 @@ def run_ours(args):
     clocks = ClockSampler(str(torch.cuda.get_device_properties(local).uuid), local)
     clocks.start()
     launches0 = native.kernel_launches()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    e1.synchronize()
+    ms = timed_steps(step, stream, args.steps, flush)
     launches = native.kernel_launches() - launches0
-    ms = e0.elapsed_time(e1)
     barrier()
     clk = clocks.stop()
     ms_max = sharding.max_over_ranks(ms, dist, "cuda")
-    value = world * B * args.steps / (ms_max / 1000.0)
+    value = n_job * args.steps / (ms_max / 1000.0)
 
     # roofline of the dominant kernel: per-launch CUDA-event times of one step
     ctx.profile_begin()
@@ -455,18 +591,9 @@ def run_ours(args):
     flops = vision_kernel_flops(B, N, tokens)
     dom = max((k for k in prof if k in flops), key=lambda k: prof[k][1])
     cnt, tot = prof[dom]
-    peaks = measured_peaks()
-    peak = peaks.get("bf16_tflops_sustained")
-    peak_src = "measured (bf16 cuBLAS, sustained)" if peak else "fallback"
-    if not peak:
-        peak = 1400.0
+    peak, peak_src = tensor_peak()
     achieved = flops[dom] / (tot / cnt / 1000.0) / 1e12
-    traffic = None
-    try:
-        tr = json.load(open(os.path.join(ROOT, "profiles", "traffic_per_launch.json")))
-        traffic = tr.get(dom, {}).get("bytes_per_launch_b64") if B == 64 else None
-    except Exception:
-        pass
+    traffic = traffic_per_launch(dom, "bytes_per_launch_b64") if B == 64 else None
     # split-operand factor: executed tensor FLOPs per algorithmic FLOP (three S products and
     # four P*V products for attention; two or one terms for the QAT linears)
     factor = {"attention": 3.5}.get(dom, 1.0 if args.quant == "calibrated" else 2.0)
@@ -488,8 +615,7 @@ def run_ours(args):
                           + ("1x" if args.quant == "calibrated" else "2x") + " that on the tensor pipe"}
 
     # end to end through the C ABI with pinned host buffers
-    out_host = [np.empty((tokens, TEXT), np.float32) for _ in range(B)]
-    out_pin = torch.empty((B, tokens, TEXT), dtype=torch.float32).pin_memory()
+    out_pin = torch.empty((max(B, 1), tokens, TEXT), dtype=torch.float32).pin_memory()
     out_host = [out_pin[i].numpy() for i in range(B)]
     in_host = [pix_host[i].numpy() for i in range(B)]
     ctx.vision_embed(in_host, max_soft, layers, outs=out_host)
@@ -500,38 +626,38 @@ def run_ours(args):
     for _ in range(k_e2e):
         ctx.vision_embed(in_host, max_soft, layers, outs=out_host)
     t_e2e = time.perf_counter() - t0
-    e2e_value = world * B * k_e2e / sharding.max_over_ranks(t_e2e, dist, "cuda")
+    e2e_value = n_job * k_e2e / sharding.max_over_ranks(t_e2e, dist, "cuda")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        s, desc = cpu_vision_sample(threads, args.quant)
-        cpu = {"value": 1.0 / s, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc}
+        rate, _, desc = cpu_rate(lambda: CpuVisionSteps(threads, args.quant), 16, 1.0, 16)
+        cpu = {"value": rate, "unit": "images/s", "cores": threads, "kind": "port", "sample": desc}
 
     sweep = qat_sweep(native, syn, peak) if rank == 0 else None
+    cfg0 = qat_cfg0(native, syn) if rank == 0 and not args.no_cpu_baseline else None
     audio = None
     if not args.no_audio:
         ctx.close()
-        audio = run_audio(args, native.Context, native, syn, rank, world, dist, barrier)
+        audio = run_audio(args, native, syn, rank, world, dist, barrier, flush)
 
     if rank == 0:
         line = {
-            "impl": "g4m", "metric": "images/s (vision tower 768x768, 16 layers, + embedder)", "value": value,
+            "impl": "g4m", "metric": VISION_METRIC, "value": value,
             "unit": "images/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": args.scaling,
+            "vs_baseline": None,
             "dtype": ("f32-grade (fp16 hi/lo split operands on tcgen05, f32 accumulate)" if args.quant == "none" else
                       "int8 activation codes x int8 weights on tcgen05 (exact in fp16), f32 accumulate"),
             "data": "synthetic (seeded U[0,1] pixels, random-init weights with the reference dtypes)",
-            "config": {"workload": f"batched vision: {B} images/GPU of 768x768 (2304 patches, 256 tokens), 16 layers",
-                       "images_per_gpu": B, "image": "768x768", "layers": layers, "parallelism": f"dp{world} (replicas)",
-                       "l2": "inputs larger than L2 (pixels %.0f MB per GPU per step)" % (B * H * Wd * 3 * 4 / 1e6),
-                       "activation_quant": QUANT_DESC[args.quant]},
+            "config": dict(vision_config(args, world), images_this_rank=B),
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": B * H * Wd * 3 * 4,
                     "d2h_bytes_per_step": B * tokens * TEXT * 4},
             "gpu_launches": launches,
             "roofline": roofline,
             "qat_linear": qat_linear,
             "qat_linear_sweep": sweep,
+            "qat_cfg0": cfg0,
             "kernel_ms_per_step": kernel_ms,
             "cpu_baseline": cpu,
             "clocks": clk,
@@ -551,10 +677,12 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--batch", type=int, default=64, help="images per GPU per step")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong: --images / --clips are the job's totals, sharded over the ranks; weak: per GPU")
+    ap.add_argument("--images", type=int, default=64, help="images in the job (strong) or per GPU (weak)")
+    ap.add_argument("--clips", type=int, default=128, help="audio clips in the job (strong) or per GPU (weak)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-audio", action="store_true", help="skip the batched-audio half of the metric")
-    ap.add_argument("--clips", type=int, default=128, help="audio clips per GPU per step")
     ap.add_argument("--quant", default="none", choices=["none", "calibrated"],
                     help="static input-activation quantisation of the QAT linears")
     args = ap.parse_args()

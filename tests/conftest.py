@@ -131,3 +131,24 @@ def assert_within_envelope(ref, got, envelope, what="", factor=1.5):
     assert (1 - g_cos) <= factor * (1 - e_cos) + 1e-4, msg
     assert g_med <= factor * e_med + 1e-5, msg
     return g_ok, g_cos, g_med
+
+
+def report(name, **kv):
+    print(f"{name}: " + ", ".join(f"{k} {v:.3e}" if isinstance(v, float) else f"{k} {v}" for k, v in kv.items()))
+
+
+def assert_float64_envelope(oracle_out, device_out, f64_out, what):
+    """North-star bound against the oracle, or the device no farther from the
+    float64 evaluation than twice the oracle is."""
+    assert np.isfinite(device_out).all(), f"{what}: non-finite output"
+    cos, ma = row_metrics(oracle_out, device_out)
+    d_cos, d_ma = row_metrics(f64_out, device_out)
+    o_cos, o_ma = row_metrics(f64_out, oracle_out)
+    report(what, dev_vs_oracle_cos=cos, dev_vs_oracle_maxabs=ma, dev_vs_f64_cos=d_cos, dev_vs_f64_maxabs=d_ma,
+            oracle_vs_f64_cos=o_cos, oracle_vs_f64_maxabs=o_ma)
+    if cos >= COS_MIN and ma <= MAXABS_RMS:
+        return cos, ma, d_ma, o_ma
+    assert d_ma <= 2 * o_ma and (1 - d_cos) <= 2 * (1 - o_cos) + 1e-9, (
+        f"{what}: device vs oracle cos {cos:.6f} max-abs/RMS {ma:.3e} misses the bound, and the device is farther "
+        f"from float64 (cos {d_cos:.7f}, max-abs/RMS {d_ma:.3e}) than 2x the oracle (cos {o_cos:.7f}, {o_ma:.3e})")
+    return cos, ma, d_ma, o_ma

@@ -2,20 +2,20 @@
 -> embedder) against the oracle's restatement of the reference CPU twins.
 
 Tolerances (north star): per-row cosine >= 0.999 and max-abs <= 1e-2 * RMS.
-The random-init tower amplifies relative perturbations by about 1.6x per
-layer, so two fp32 implementations with different summation orders drift
-apart to a max-abs of a few 1e-2 * RMS after 16 propagated layers while the
-cosine stays above 0.9999.  The max-abs bound is therefore checked per layer
+The random-init tower amplifies relative perturbations layer over layer, so
+two f32-grade implementations with different summation orders drift apart
+after many propagated layers.  The bound is asserted per kernel, per layer
 (anchored, like the reference's gpuAnchored probes) and on stacks of up to
-four layers; the 16-layer propagated check asserts the cosine bound and a
-max-abs bound of 0.2 * RMS.
+four layers; the 16-layer propagated run must meet it or be no farther from a
+float64 evaluation than twice the oracle is (tests/test_gpu_full_config.py
+holds the same checks at the full 768 x 768 configuration).
 """
 import os
 
 import numpy as np
 import pytest
 
-from conftest import assert_parity, row_metrics
+from conftest import assert_float64_envelope, assert_parity, row_metrics
 
 pytestmark = pytest.mark.gpu
 
@@ -69,6 +69,9 @@ def test_vision_full_size_anchored_layer(vis, oracle, syn):
 
 
 def test_vision_tc_attention_matches_simt(vis, native, syn, monkeypatch):
+    """Consistency of the two device attention paths (tcgen05 and the fp32
+    SIMT kernel) on two 768 x 768 images; parity with the oracle is checked
+    by the anchored and end-to-end tests."""
     c, W, path = vis
     pix = [syn.image_pixels(s, 768, 768) for s in range(2)]
     a, _ = c.vision_embed(pix, 280, 2)
@@ -132,8 +135,9 @@ def vis16(native, syn, tmp_path_factory):
 
 def test_vision_16_layers_propagated(vis16, oracle, syn):
     """Full 16-layer stack on a 288 x 288 image (324 patches, 36 tokens)."""
+    import np_ref
     c, W = vis16
-    pix, ref, _, _ = _oracle_case(oracle, syn, W, 288, 288, 36, 16, seed=7)
+    pix, ref, patches, pos = _oracle_case(oracle, syn, W, 288, 288, 36, 16, seed=7)
     outs, _ = c.vision_embed([pix], 36, 16)
-    cos, ma = assert_parity(ref, outs[0], cos_min=0.999, maxabs=0.2, what="16 layers propagated")
-    print(f"16-layer propagated: min row cos {cos:.7f}, max-abs/RMS {ma:.3e}")
+    ref64 = np_ref.vision_embed(W, patches, pos, 18, 18, layer_count=16)
+    assert_float64_envelope(ref, outs[0], ref64, "vision 288x288, 16 layers propagated")
