@@ -8,10 +8,11 @@
 // Operands are fp16 hi/lo planes, so every product is split into three
 // tensor-core terms (hi*hi + hi*lo + lo*hi) for fp32-grade scores and
 // outputs:   S = Qh Kh^T + Qh Kl^T + Ql Kh^T,   O += (Ph + Pl) (Vh + Vl).
-// A tcgen05.mma costs about the same for any N <= 128, so P*V stacks the V
-// hi and lo planes into one N = 128 operand: Ph [Vh | Vl] and Pl [Vh | Vl]
-// accumulate into 128 TMEM columns whose two halves are summed at the end
-// (two instructions per 16 keys instead of three N = 64 ones).
+// An N = 64 tcgen05.mma takes three quarters of the time of an N = 128 one
+// (measured: 48 against 64 cycles), so P*V stacks the V hi and lo planes into
+// one N = 128 operand: Ph [Vh | Vl] and Pl [Vh | Vl] accumulate into 128 TMEM
+// columns whose two halves are summed at the end (two instructions per 16
+// keys instead of three N = 64 ones).
 //
 // One CTA per (image*head, 256 queries) = two 128-query tiles A and B that
 // share every K / V tile, 320 threads:
@@ -29,7 +30,8 @@
 // [32c+16, 32c+32), and the P*V MMA reads P straight from TMEM (A operand),
 // so P never touches shared memory.  O accumulates in TMEM across key tiles; a
 // row's running max is raised (and its O row rescaled in TMEM) only when a
-// tile's max exceeds it by more than 2^8, so P <= 256 and the rescale is rare.
+// tile's max exceeds it by more than 2^8, so P <= 2^(8 + kPShift) and the
+// rescale is rare.
 // The next S of a tile overwrites its P columns, so the MMA warp issues it
 // only after that tile's P*V has completed (waits overlap the other tile's
 // MMAs).
@@ -55,7 +57,8 @@ constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t O_COL = 256;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescale = 8.0f;       // log2 of the largest P before a rescale
+constexpr float kRescale = 8.0f;       // log2 growth of a row's max that triggers a rescale
+constexpr float kPShift = 7.0f;        // log2 of P at a row's running max (so P <= 2^15 < fp16 max)
 static_assert(SMEM_ALLOC + 512 <= 232448, "dynamic + static shared memory exceeds 227 KB per block");
 
 __device__ __forceinline__ float ex2(float x) {
@@ -107,6 +110,16 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <bool ACC>
+__device__ __forceinline__ void mma_f16_ts_c(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "n"(ACC ? 1 : 0)
       : "memory");
 }
 
@@ -196,20 +209,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id_s = idesc_f16_f32(128, KT);
       constexpr uint32_t id_pv = idesc_f16_f32(128, 2 * HD);
       bool ok = mbar_wait(&b_q, 0, err, kErrWaitFull, &abort_flag);
+      // Descriptor of the tile at byte offset 0 of the aligned region; every
+      // operand descriptor below is this plus a constant offset.
+      const uint64_t dbase = desc_k_sw128(smem_u32(sm));
       // S_t(j) = Q_t K_j^T into TMEM columns [128 t, 128 t + 128)
       auto issue_s = [&](int t, int j) -> bool {
         const int s = j & 1;
         if (!mbar_wait(&b_kvf[s], (j >> 1) & 1, err, kErrWaitFull, &abort_flag)) return false;
         tc_fence_after();
-        const uint32_t qh = smem_u32(sm + Q_OFF + 2 * t * TILE_BYTES), ql = qh + TILE_BYTES;
-        const uint32_t kh = smem_u32(sm + KV_OFF + s * KV_STAGE), kl = kh + TILE_BYTES;
+        const uint64_t qh = desc_add(dbase, Q_OFF + 2 * t * TILE_BYTES), ql = desc_add(qh, TILE_BYTES);
+        const uint64_t kh = desc_add(dbase, KV_OFF + s * KV_STAGE), kl = desc_add(kh, TILE_BYTES);
         const uint32_t d = tmem + t * KT;
+        mma_f16_ss_c<false>(d, qh, kh, id_s);
+        mma_f16_ss_c<true>(d, qh, kl, id_s);
+        mma_f16_ss_c<true>(d, ql, kh, id_s);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const uint64_t dq = desc_k_sw128(qh + kk * 32), dk = desc_k_sw128(kh + kk * 32);
-          mma_f16_ss(d, dq, dk, id_s, kk > 0 ? 1u : 0u);
-          mma_f16_ss(d, dq, desc_k_sw128(kl + kk * 32), id_s, 1u);
-          mma_f16_ss(d, desc_k_sw128(ql + kk * 32), dk, id_s, 1u);
+        for (int kk = 1; kk < HD / 16; ++kk) {
+          mma_f16_ss_c<true>(d, desc_add(qh, kk * 32), desc_add(kh, kk * 32), id_s);
+          mma_f16_ss_c<true>(d, desc_add(qh, kk * 32), desc_add(kl, kk * 32), id_s);
+          mma_f16_ss_c<true>(d, desc_add(ql, kk * 32), desc_add(kh, kk * 32), id_s);
         }
         mma_commit(&b_s[t]);
         return true;
@@ -219,14 +237,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](int t, int j) -> bool {
         if (!mbar_wait(&b_p[t], j & 1, err, kErrWaitFull, &abort_flag)) return false;
         tc_fence_after();
-        const uint32_t v = smem_u32(sm + KV_OFF + (j & 1) * KV_STAGE + 2 * TILE_BYTES);
+        const uint64_t v = desc_add(dbase, KV_OFF + (j & 1) * KV_STAGE + 2 * TILE_BYTES);
         const uint32_t d = tmem + O_COL + t * 2 * HD, a = tmem + t * KT;
+        mma_f16_ts(d, a, v, id_pv, j > 0 ? 1u : 0u);  // the first product of the tile starts O at j = 0
+        mma_f16_ts_c<true>(d, a + 16, v, id_pv);
 #pragma unroll
-        for (int kk = 0; kk < KT / 16; ++kk) {
-          const uint64_t dv = desc_k_sw128(v + (kk >> 2) * TILE_BYTES + (kk & 3) * 32);
+        for (int kk = 1; kk < KT / 16; ++kk) {
+          const uint64_t dv = desc_add(v, (kk >> 2) * TILE_BYTES + (kk & 3) * 32);
           const uint32_t ah = a + 32 * (kk >> 1) + 8 * (kk & 1);
-          mma_f16_ts(d, ah, dv, id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-          mma_f16_ts(d, ah + 16, dv, id_pv, 1u);
+          mma_f16_ts_c<true>(d, ah, dv, id_pv);
+          mma_f16_ts_c<true>(d, ah + 16, dv, id_pv);
         }
         mma_commit(&b_pv[t]);
         return true;
@@ -310,11 +330,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (need) m = mt;
         }
       }
-      // pass 2: P = 2^(s log2e - m) chunk by chunk (32 keys); chunks 0 and 1
+      // pass 2: P = 2^(s log2e - m + kPShift) chunk by chunk (32 keys); chunks 0 and 1
       // come from pass 1's registers, chunks 2 and 3 are reloaded while
       // chunks 0 and 1 are converted; P hi / lo go back into the chunk's own
       // columns.
-      const float mneg = -m;
+      // P carries a factor 2^kPShift (the row sum carries it too, so it cancels
+      // in O / l): keys well below the row's maximum keep their lo plane out of
+      // the fp16 subnormal range.
+      const float mneg = kPShift - m;
       float rp[4] = {0.f, 0.f, 0.f, 0.f};  // four independent sum chains
       tmem_ld32_nw(s_col + 64, sr + 64);    // chunk 2
 #pragma unroll

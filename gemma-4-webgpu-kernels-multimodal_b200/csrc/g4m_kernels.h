@@ -51,6 +51,13 @@ struct GemmOperands {
 
 struct GemmArgs {
   int M, N, K;
+  // K chunking of the accumulation, in 64-wide k-blocks (0: one chunk).  The
+  // tensor core adds each product into the running f32 accumulator with a
+  // truncating alignment, so the accumulation error grows with the
+  // accumulator's magnitude; with chunks, every chunk starts from zero in a
+  // second TMEM buffer and the epilogue adds it into the tile's total with
+  // round-to-nearest f32 adds.
+  int chunk_kb;
   const float* col_scale;  // [N] per-output-channel weight scale (may be null for EPI_F32)
   float row_scale;         // 1, or s_in when A holds integer codes
   float row_scale_b;       // amode 1/2: s_in of region / half 1 (else = row_scale)

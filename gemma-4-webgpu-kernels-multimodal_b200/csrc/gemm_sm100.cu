@@ -248,14 +248,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
       constexpr uint32_t idesc_half = idesc_f16_f32(BM, BN / 2);
-      uint32_t it = 0, t = 0;
+      // K chunks of every tile go to the two TMEM buffers alternately, in
+      // one sequence over all tiles of this CTA: chunk k lands in buffer k & 1
+      // (its (k >> 1)-th use).  The epilogue keeps each tile's running total
+      // in the buffer of its latest chunk (chunk_kb == 0: one chunk per tile,
+      // plain double buffering across tiles).
+      uint32_t it = 0, k = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++t) {
-        const uint32_t buf = t & 1, use = t >> 1;
-        if (!mbar_wait(&bar_acce[buf], (use & 1) ^ 1, a.err, kErrWaitAccEmpty, &abort_flag)) break;
-        tc_fence_after();
-        const uint32_t d = tmem_base + buf * BN;
+      const uint64_t dbase = desc_k_sw128(smem_u32(smem));
+      const int chunk_len = a.chunk_kb > 0 ? a.chunk_kb : kblocks;
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+        uint32_t b = 0, d = tmem_base;
+        int left = 0;  // k-blocks left in the current chunk
         for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const bool first = left == 0;
+          if (first) left = chunk_len;
+          const bool last = --left == 0 || kb + 1 == kblocks;
+          if (first) {
+            b = k & 1;
+            if (!mbar_wait(&bar_acce[b], ((k >> 1) & 1) ^ 1, a.err, kErrWaitAccEmpty, &abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            d = tmem_base + b * BN;
+          }
           const int s = it % C::STAGES;
           const uint32_t r = it / C::STAGES;
           if (!mbar_wait(&bar_full[s], r & 1, a.err, kErrWaitFull, &abort_flag)) {
@@ -263,26 +280,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a0 = smem_u32(sA(s, 0)), b0 = smem_u32(sB(s, 0));
+          const uint64_t ga = desc_add(dbase, s * C::STAGE_BYTES);   // A (hi) of stage s
+          const uint64_t gb = desc_add(ga, C::NA * C::A_BYTES);       // B (hi) of stage s
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t da0 = desc_k_sw128(a0 + k * 32), db0 = desc_k_sw128(b0 + k * 32);
+            const uint64_t da0 = desc_add(ga, k * 32), db0 = desc_add(gb, k * 32);
+            const uint32_t acc = (!first || k > 0) ? 1u : 0u;
             if (AMODE == 2) {
               // halves of the B tile (rows [0, BN/2) and [BN/2, BN)) against their own codes
-              const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
               mma_f16_ss(d, da0, db0, idesc_half, acc);
-              mma_f16_ss(d + BN / 2, desc_k_sw128(smem_u32(sA(s, 1)) + k * 32),
-                         desc_k_sw128(b0 + (BN / 2) * 128 + k * 32), idesc_half, acc);
+              mma_f16_ss(d + BN / 2, desc_add(ga, C::A_BYTES + k * 32), desc_add(gb, (BN / 2) * 128 + k * 32),
+                         idesc_half, acc);
               continue;
             }
-            mma_f16_ss(d, da0, db0, idesc, (kb > 0 || k > 0) ? 1u : 0u);
-            if (TERMS >= 2) mma_f16_ss(d, desc_k_sw128(smem_u32(sA(s, 1)) + k * 32), db0, idesc, 1u);
-            if (TERMS == 3) mma_f16_ss(d, da0, desc_k_sw128(smem_u32(sB(s, 1)) + k * 32), idesc, 1u);
+            if (k == 0) mma_f16_ss(d, da0, db0, idesc, acc);
+            else mma_f16_ss_c<true>(d, da0, db0, idesc);
+            if (TERMS >= 2) mma_f16_ss_c<true>(d, desc_add(ga, C::A_BYTES + k * 32), db0, idesc);
+            if (TERMS == 3) mma_f16_ss_c<true>(d, da0, desc_add(gb, C::B_BYTES + k * 32), idesc);
           }
           mma_commit(&bar_empty[s]);
+          if (last) {
+            mma_commit(&bar_accf[b]);
+            ++k;
+            left = 0;
+          }
         }
-        if (!ok) break;
-        mma_commit(&bar_accf[buf]);
       }
       // Let the last stage-release commits land before the CTA can exit.
       if (ok && !abort_flag) {
@@ -299,12 +321,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int eg = (warp - 2) >> 2;
     const int row_in_tile = 32 * q + lane;
     uint4* stage = reinterpret_cast<uint4*>(smem + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_STAGE);
-    uint32_t t = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++t) {
-      const uint32_t buf = t & 1, use = t >> 1;
+    const int nchunks = a.chunk_kb ? (kblocks + a.chunk_kb - 1) / a.chunk_kb : 1;
+    const uint32_t lq = (uint32_t)(32 * q) << 16;
+    uint32_t k = 0;  // chunks consumed so far (the MMA warp's sequence)
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       // tcgen05.ld is warp-collective: every lane takes the same branch.
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[buf], use & 1, a.err, kErrWaitAccFull, &abort_flag));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[k & 1], (k >> 1) & 1, a.err, kErrWaitAccFull, &abort_flag));
       if (!ok) break;
+      ++k;
+      // Every later chunk of the tile: total (previous buffer) + chunk (its
+      // buffer) with round-to-nearest f32 adds, written into the chunk's
+      // buffer; the previous buffer is handed back as soon as it is read.
+      for (int c = 1; c < nchunks && ok; ++c, ++k) {
+        const uint32_t cb = k & 1, tb_ = cb ^ 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[cb], (k >> 1) & 1, a.err, kErrWaitAccFull, &abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        constexpr int COLS = BN / kEpiGroups;  // this warpgroup's columns
+#pragma unroll
+        for (int p = 0; p < COLS / 32; ++p) {
+          const int col = eg * COLS + 32 * p;
+          uint32_t x[32], y[32];
+          tmem_ld32_raw(tmem_base + lq + tb_ * BN + col, x);
+          tmem_ld32_raw(tmem_base + lq + cb * BN + col, y);
+          tmem_wait_ld_all();
+          if (p == COLS / 32 - 1) {  // the previous total is fully read: its buffer may take the next chunk
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_acce[tb_]);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) y[i] = __float_as_uint(__uint_as_float(x[i]) + __uint_as_float(y[i]));
+          tmem_st32(tmem_base + lq + cb * BN + col, y);
+        }
+        tmem_wait_st_all();
+      }
+      if (!ok) break;
+      const uint32_t buf = (k - 1) & 1;  // the buffer holding the tile's total
       tc_fence_after();
       const int mb = tile / tiles_n, nb = tile % tiles_n;
       const uint32_t tb = tmem_base + ((uint32_t)(32 * q) << 16) + buf * BN;
@@ -640,9 +693,11 @@ static cudaError_t launch_t(const GemmOperands& op, const GemmArgs& args, cudaSt
   return cudaGetLastError();
 }
 
-cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args, cudaStream_t st,
+cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args_in, cudaStream_t st,
                         int max_ctas, int amode) {
-  if (args.K % BK != 0 || args.N % bn != 0 || args.M <= 0) return cudaErrorInvalidValue;
+  if (args_in.K % BK != 0 || args_in.N % bn != 0 || args_in.M <= 0) return cudaErrorInvalidValue;
+  GemmArgs args = args_in;
+  if (terms == 1) args.chunk_kb = 0;  // integer codes: the products and their sums are exact integers
 #define G4M_CASE(BN_, T_, E_, A_) \
   if (bn == BN_ && terms == T_ && epi == E_ && amode == A_) return launch_t<BN_, T_, E_, A_>(op, args, st, max_ctas);
   G4M_CASE(256, 1, EPI_F32, 0)

@@ -380,12 +380,21 @@ static int ensure_vision_buffers(Device& d, int B, int N, long E) {
     if (e_ != cudaSuccess) return fail(G4M_E_CUDA, std::string(#x) + ": " + cudaGetErrorString(e_)); \
   } while (0)
 
+// K chunk of the vision tower's and the QAT linear's fp16 hi/lo GEMMs, in
+// 64-wide k-blocks (GemmArgs::chunk_kb): two chunks per K = 768 linear,
+// eight for K = 3072.  Measured on the 768 x 768 image through 16 propagated
+// layers, the device's distance to a float64 evaluation drops from 2.4x to
+// 1.3x the reference f32 arithmetic's own distance, for ~5 % of the tower's
+// time.  GEMMs on integer codes accumulate exact integers and need none.
+constexpr int kVisionChunkKb = 6;
+
 static GemmArgs base_args(Device& d, int M, int N, int K) {
   GemmArgs a;
   memset(&a, 0, sizeof(a));
   a.M = M;
   a.N = N;
   a.K = K;
+  a.chunk_kb = kVisionChunkKb;
   a.row_scale = 1.0f;
   a.row_scale_b = 1.0f;
   a.row_scale_c = 1.0f;

@@ -118,16 +118,16 @@ def audio_cfg2(native, syn, oracle, tmp_path_factory):
 
 def test_audio_cfg2_every_layer_anchored(audio_cfg2):
     """All 12 conformer layers on the 10 s clip's 250 rows, each fed the
-    oracle's input of that layer, at the north-star bound."""
+    oracle's input of that layer: the north-star bound, or -- where the
+    oracle's own packed-code sums (sum code*a - zp*sum a, which cancel) put it
+    farther than the bound from float64 -- no farther from float64 than twice
+    the oracle."""
     import np_ref
     a = audio_cfg2
     for i in range(12):
         got = a["c"].audio_layers(a["hid"][i], [250], i, 1)
-        cos, ma = assert_parity(a["hid"][i + 1], got, what=f"audio layer {i} anchored (250 rows)")
         ref64 = np_ref.audio_layer(a["W"], i, a["hid"][i])
-        _, d64 = row_metrics(ref64, got)
-        _, o64 = row_metrics(ref64, a["hid"][i + 1])
-        report(f"audio layer {i}", cos=cos, maxabs=ma, dev_vs_f64=d64, oracle_vs_f64=o64)
+        assert_float64_envelope(a["hid"][i + 1], got, ref64, f"audio layer {i} anchored (250 rows)")
 
 
 def test_audio_cfg2_end_to_end(audio_cfg2):
