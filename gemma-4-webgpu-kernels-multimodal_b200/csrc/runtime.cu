@@ -746,30 +746,34 @@ int g4m_qat_linear(g4m_ctx* ctx, int di, const float* x, int rows, int in, int o
   if (!(bits == 0 || bits == 2 || bits == 4 || bits == 8)) return fail(G4M_E_ARG, "bits must be 0 (int8) or 2/4/8");
   if (bits && (in * bits) % 32 != 0) return fail(G4M_E_SHAPE, "packed QAT row is not byte and u32 aligned.");
   if (rows == 0) return G4M_OK;
-  g4m_linear* lin = nullptr;
-  int rc = g4m_linear_prepare(ctx, di, w, bits, out, in, w_scale, s_in, s_out, bias, &lin);
-  if (rc) return rc;
-  Device& d = *lin->d;
+  Device& d = *ctx->devs[di];
   std::lock_guard<std::mutex> lk(d.mu);
   cudaSetDevice(d.id);
-  DevBuf xb, yb;
-  if (ensure(xb, (size_t)rows * in * 4) || ensure(yb, (size_t)rows * out * 4)) {
-    g4m_linear_free(lin);
-    return fail(G4M_E_CUDA, "activation allocation failed");
-  }
-  rc = G4M_OK;
-  if (cudaMemcpyAsync(xb.p, x, (size_t)rows * in * 4, cudaMemcpyHostToDevice, d.st) != cudaSuccess)
-    rc = fail(G4M_E_CUDA, "input upload failed");
-  if (!rc)
-    rc = qat_linear_device(d, lin->w16, lin->scale, lin->bias, lin->w_raw, bits, rows, in, out, s_in, s_out,
-                           (const float*)xb.p, (float*)yb.p, lin->a_hi, lin->a_lo, d.st);
-  if (!rc && cudaMemcpyAsync(y, yb.p, (size_t)rows * out * 4, cudaMemcpyDeviceToHost, d.st) != cudaSuccess)
-    rc = fail(G4M_E_CUDA, "output download failed");
-  if (!rc) rc = finish(d, d.st);
-  release(xb);
-  release(yb);
-  g4m_linear_free(lin);
-  return rc;
+  (void)cudaGetLastError();
+  // One call of the reference's runner (runQatI8LinearWebGpu) takes its
+  // weights with the activations, so they are uploaded and converted here on
+  // every call; the device buffers persist across calls (grown on demand),
+  // everything runs on the device's stream, and the host waits once.
+  const size_t wbytes = bits ? (size_t)out * in * bits / 8 : (size_t)out * in;
+  const bool tc = qat_tensor_core_shape(in, out);
+  if (ensure(d.qw_raw, wbytes) || ensure(d.qscale, (size_t)out * 4) || (bias && ensure(d.qbias, (size_t)out * 4)) ||
+      ensure(d.qx, (size_t)rows * in * 4) || ensure(d.qy, (size_t)rows * out * 4) ||
+      (tc && ensure(d.qw16, (size_t)out * in * 2)))
+    return fail(G4M_E_CUDA, "QAT linear buffer allocation failed");
+  cudaStream_t st = d.st;
+  if (cudaMemcpyAsync(d.qw_raw.p, w, wbytes, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync(d.qscale.p, w_scale, (size_t)out * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      (bias && cudaMemcpyAsync(d.qbias.p, bias, (size_t)out * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) ||
+      cudaMemcpyAsync(d.qx.p, x, (size_t)rows * in * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return fail(G4M_E_CUDA, "QAT linear upload failed");
+  if (tc) G4M_RUN("prep_w", prep_w(d.qw_raw.p, bits ? 1 : 0, bits, out, in, nullptr, (__half*)d.qw16.p, nullptr, st));
+  int rc = qat_linear_device(d, tc ? (const __half*)d.qw16.p : nullptr, (const float*)d.qscale.p,
+                             bias ? (const float*)d.qbias.p : nullptr, d.qw_raw.p, bits, rows, in, out, s_in, s_out,
+                             (const float*)d.qx.p, (float*)d.qy.p, d.qa_hi, d.qa_lo, st);
+  if (rc) return rc;
+  if (cudaMemcpyAsync(y, d.qy.p, (size_t)rows * out * 4, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return fail(G4M_E_CUDA, "output download failed");
+  return finish(d, st);
 }
 
 int g4m_linear_prepare(g4m_ctx* ctx, int di, const void* w, int bits, int out, int in, const float* w_scale, float s_in,

@@ -142,6 +142,8 @@ struct Device {
   AudioBuffers ab;
   LayoutCache vlc;
   DevBuf io_in, io_out, io_src, io_tmp;  // batch staging; io_src / io_tmp: source images and resize rows
+  // g4m_qat_linear's per-call operands, grown on demand and reused by later calls
+  DevBuf qw_raw, qw16, qscale, qbias, qx, qy, qa_hi, qa_lo;
   long last_vision_rows = 0;
   long last_audio_rows = 0;
   int aw_mel_sr = 0;  // sampling rate the mel filter bank was built for
@@ -163,7 +165,8 @@ struct Device {
     allocs.clear();
     DevBuf* bufs[] = {&vb.h, &vb.y, &vb.h0, &vb.a_hi, &vb.a_lo, &vb.a_c, &vb.o_hi, &vb.o_lo, &vb.g_hi, &vb.g_lo,
                       &vb.q_hi, &vb.q_lo, &vb.k_hi, &vb.k_lo, &vb.vt_hi, &vb.vt_lo, &vb.e_hi, &vb.e_lo,
-                      &vlc.pos_xy, &vlc.rope, &vlc.pool, &io_in, &io_out, &io_src, &io_tmp};
+                      &vlc.pos_xy, &vlc.rope, &vlc.pool, &io_in, &io_out, &io_src, &io_tmp, &qw_raw, &qw16,
+                      &qscale, &qbias, &qx, &qy, &qa_hi, &qa_lo};
     for (DevBuf* b : bufs) release(*b);
     DevBuf* abufs[] = {&ab.samples, &ab.sample_off, &ab.sample_len, &ab.frame_off, &ab.frames, &ab.feats,
                        &ab.fmask, &ab.t0_off, &ab.t0_len, &ab.l0, &ab.l0mask, &ab.t1_off, &ab.t1_len, &ab.l1,
