@@ -381,9 +381,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int wq0 = q0 + t * QT + 32 * qw;  // query row of lane 0
       const size_t ostride = (size_t)heads * HD * 2;
       const size_t obase = ((size_t)img * n + wq0) * (size_t)(heads * HD) + head * HD;
-      // one plane at a time (hi, lo or codes), the O columns re-read from
-      // TMEM chunk by chunk so that only the plane's eight words stay live
-      const int planes = s_code != 0.0f ? 1 : 2;
+      if (s_code != 0.0f) {
+        // signed-byte codes for the o_proj input scale: 64 bytes per row
+        // (row stride heads * 64 bytes)
+        uint4 w[4];
+#pragma unroll
+        for (int h = 0; h < HD / 16; ++h) {
+          uint32_t ov[16], ol[16];
+          tmem_ld16_nw(o_col + 16 * h, ov);       // P * Vh
+          tmem_ld16_nw(o_col + HD + 16 * h, ol);  // P * Vl
+          tmem_wait_ld();
+          uint32_t b4[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            uint32_t x = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float v = (__uint_as_float(ov[4 * u + e]) + __uint_as_float(ol[4 * u + e])) * inv;
+              x |= ((uint32_t)(int)srq_code(v, s_code, inv_code) & 0xFFu) << (8 * e);
+            }
+            b4[u] = x;
+          }
+          w[h] = make_uint4(b4[0], b4[1], b4[2], b4[3]);
+        }
+        warp_store_block<64>(stage, w, reinterpret_cast<char*>(o_hi) + obase, (size_t)heads * HD, n - wq0, lane);
+      }
+      // hi and lo planes one at a time, the O columns re-read from TMEM chunk
+      // by chunk so that only the plane's eight words stay live
+      const int planes = s_code != 0.0f ? 0 : 2;
 #pragma unroll 1
       for (int pl = 0; pl < planes; ++pl) {
         uint4 w[8];
@@ -401,18 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int i = 8 * half + 2 * u;
               const float x0 = (__uint_as_float(ov[i]) + __uint_as_float(ol[i])) * inv;
               const float x1 = (__uint_as_float(ov[i + 1]) + __uint_as_float(ol[i + 1])) * inv;
-              if (s_code != 0.0f) {  // integer codes for the o_proj input scale
-                union {
-                  __half2 h2;
-                  uint32_t wd;
-                } cv;
-                cv.h2 = __floats2half2_rn(srq_code(x0, s_code, inv_code), srq_code(x1, s_code, inv_code));
-                q4[u] = cv.wd;
-              } else {
-                uint32_t hw, lw;
-                split2_f16(x0, x1, hw, lw);
-                q4[u] = pl ? lw : hw;
-              }
+              uint32_t hw, lw;
+              split2_f16(x0, x1, hw, lw);
+              q4[u] = pl ? lw : hw;
             }
             w[2 * h + half] = make_uint4(q4[0], q4[1], q4[2], q4[3]);
           }

@@ -32,9 +32,10 @@ enum Epi : int {
 
 // Static input-activation quantisation (input_activation_scale s != 0,
 // srqScalar in src/kernels/qat.ts:489-492): an operand producer stores the
-// integer code clamp(round(x / s), -128, 127) (exact in fp16) in place of the
-// hi/lo split, the GEMM runs one term on the codes and its epilogue scales by
-// s.  Projections that share an input (q / k / v, gate / up) keep their own
+// integer code clamp(round(x / s), -128, 127) as a signed byte in place of
+// the hi/lo split (a code plane of K bytes per row), the GEMM runs one
+// kind::i8 term on the codes against int8 weights with exact int32
+// accumulation, and its epilogue scales by s.  Projections that share an input (q / k / v, gate / up) keep their own
 // s, so their GEMM selects the code plane per output region (amode):
 //   amode 0  one A for the whole GEMM (terms 1..3 as above)
 //   amode 1  one code plane per proj_width-column region, chosen per tile
@@ -90,6 +91,7 @@ struct GemmArgs {
 cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args, cudaStream_t st,
                         int max_ctas = 0, int amode = 0);
 bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
+bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows);
 // Any cols with a 16-byte-multiple row pitch `pitch_elems` (>= cols).
 bool make_tmap_f16_any(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                        uint32_t box_rows);
@@ -98,6 +100,8 @@ cudaError_t prep_a(const float* x, long rows, int cols, float s_in, const float*
                    cudaStream_t st);
 cudaError_t prep_w(const void* src, int kind, int bits, int rows, int cols, const int* map, __half* hi, __half* lo,
                    cudaStream_t st);
+cudaError_t prep_w_i8(const void* src, int kind, int bits, int rows, int cols, const int* map, int8_t* dst,
+                      cudaStream_t st);
 
 // ---------------------------------------------------------------------------
 // Row kernels (norms, residuals) -- kernels_rows.cu
@@ -113,7 +117,7 @@ struct RowArgs {
   const float* w_out;      // optional RMSNorm of the new residual (audio norm_out)
   float* h_out;            // residual output (may alias h_in)
   const float* w_next;     // optional RMSNorm producing the next GEMM operand
-  float s_in_next;         // 0: hi/lo planes.  Else integer codes for s_in_next in a_hi,
+  float s_in_next;         // 0: hi/lo planes.  Else signed-byte codes for s_in_next in a_hi (lda bytes per row),
   float s_in_b, s_in_c;    // and (when non-zero) codes for s_in_b in a_lo, for s_in_c in a_c
   __half* a_hi;
   __half* a_lo;
@@ -133,7 +137,7 @@ cudaError_t vision_pool_operand(const float* h, const int* pool_idx, int n_image
 // linear resize, 8-bit rounding, 1/255 rescale.  tmp: [h][tw][3] f32.
 cudaError_t vision_resize(const uint8_t* src, int h, int w, int c, int th, int tw, float* tmp, float* dst,
                           cudaStream_t st);
-// s_code != 0: O is stored as integer codes for the o_proj input scale (o_hi only).
+// s_code != 0: O is stored as signed-byte codes for the o_proj input scale (o_hi only, 768 bytes per row).
 cudaError_t vision_attention_simt(const __half* q_hi, const __half* q_lo, const __half* k_hi, const __half* k_lo,
                                   const __half* vt_hi, const __half* vt_lo, int bh, int n, int vt_pitch, int heads,
                                   __half* o_hi, __half* o_lo, float s_code, cudaStream_t st);

@@ -202,6 +202,28 @@ __device__ __forceinline__ void mma_f16_ss_c(uint32_t d_tmem, uint64_t adesc, ui
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::i8: signed 8-bit A and B (K = 32
+// per instruction, the same 32 bytes of a 128-byte swizzled row as K = 16 of
+// fp16), exact 32-bit integer accumulation.
+__device__ __forceinline__ void mma_i8_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+template <bool ACC>
+__device__ __forceinline__ void mma_i8_ss_c(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "n"(ACC ? 1 : 0)
+      : "memory");
+}
+
 // Shared-memory descriptor advanced by `bytes` (a multiple of 16): the start
 // address field is the low 14 bits (address >> 4), and every operand tile
 // lies below 256 KB of shared memory, so the sum never carries out of it.
@@ -283,6 +305,13 @@ __device__ __forceinline__ uint64_t desc_k_sw128(uint32_t smem_addr) {
 //   15/16 A/B major (0 = K); 17-22 N >> 3; 24-28 M >> 4.
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
   return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// Instruction descriptor, kind::i8: signed 8-bit A and B (K-major), s32 D.
+//   bits 4-5 D format (2 = s32); 7-9 A format (1 = signed 8-bit); 10-12 B
+//   format; 17-22 N >> 3; 24-28 M >> 4.
+__host__ __device__ constexpr uint32_t idesc_i8_s32(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 // Two floats -> packed fp16x2 hi and lo words (hi = fp16(x), lo = fp16(x - hi)).

@@ -31,7 +31,8 @@
 namespace g4m {
 
 constexpr int BM = 128;
-constexpr int BK = 64;
+constexpr int BK = 64;      // k-block of the fp16 GEMMs (128 bytes of a row)
+constexpr int BK_I8 = 128;  // k-block of the int8 GEMMs (the same 128 bytes)
 constexpr int kEpiGroups = 2;                       // epilogue warpgroups
 constexpr int kGemmThreads = 64 + 128 * kEpiGroups;  // producer, MMA, epilogue
 
@@ -39,8 +40,8 @@ template <int BN, int TERMS, int AMODE = 0>
 struct GemmCfg {
   static constexpr int NA = (TERMS >= 2 || AMODE == 2) ? 2 : 1;
   static constexpr int NB = TERMS == 3 ? 2 : 1;
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int A_BYTES = BM * 128;  // one 128-byte swizzled row per tile row and k-block
+  static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
   static constexpr int STAGES = (196608 / STAGE_BYTES) > 6 ? 6 : (196608 / STAGE_BYTES);
   static constexpr int EPI_STAGE = 4096;  // per epilogue warp: a 32-row x 128-byte store block
@@ -137,21 +138,29 @@ __device__ __forceinline__ void pack_f16(const float* v, uint4* o, int nwords16)
     o[c] = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
-__device__ __forceinline__ void pack_codes(const float* v, float sc, uint4 (&o)[4]) {
+// 32 floats -> srq codes as signed bytes (two 16-byte words).
+__device__ __forceinline__ void pack_codes_i8(const float* v, float sc, uint4 (&o)[2]) {
   const float inv = 1.0f / sc;
+  uint32_t w[8];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t w[4];
+  for (int i = 0; i < 8; ++i) {
+    uint32_t x = 0;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      union {
-        __half2 h;
-        uint32_t x;
-      } cv;
-      cv.h = __floats2half2_rn(srq_code(v[8 * c + 2 * u], sc, inv), srq_code(v[8 * c + 2 * u + 1], sc, inv));
-      w[u] = cv.x;
-    }
-    o[c] = make_uint4(w[0], w[1], w[2], w[3]);
+    for (int u = 0; u < 4; ++u) x |= ((uint32_t)(int)srq_code(v[4 * i + u], sc, inv) & 0xFFu) << (8 * u);
+    w[i] = x;
+  }
+  o[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  o[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// 32 accumulator columns of this warp's lanes as floats: f32 accumulators as
+// they are, s32 accumulators (int8 GEMMs) converted.
+template <bool I8>
+__device__ __forceinline__ void acc_ld32(uint32_t taddr, float* v) {
+  tmem_ld32(taddr, v);
+  if (I8) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (float)__float_as_int(v[i]);
   }
 }
 
@@ -162,6 +171,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                    const __grid_constant__ CUtensorMap mA2, GemmArgs a) {
   static_assert(AMODE == 0 || TERMS == 1, "per-region A selection runs on integer codes (one term)");
   using C = GemmCfg<BN, TERMS, AMODE>;
+  // One term means integer codes (static input quantisation) against int8
+  // weights: signed bytes, kind::i8 MMAs and exact int32 accumulation.
+  constexpr bool I8 = TERMS == 1;
+  constexpr int KBE = I8 ? BK_I8 : BK;  // elements per k-block
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bar_full[C::STAGES], bar_empty[C::STAGES], bar_accf[2], bar_acce[2];
   __shared__ uint32_t tmem_slot;
@@ -170,7 +183,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles_n = a.N / BN, tiles_m = (a.M + BM - 1) / BM, tiles = tiles_m * tiles_n;
-  const int kblocks = a.K / BK;
+  const int kblocks = a.K / KBE;
 
   if (threadIdx.x == 0) skip = *reinterpret_cast<volatile int*>(a.err) != 0;
   __syncthreads();
@@ -221,13 +234,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (AMODE == 1) {
             const int region = nb * BN / a.proj_width;
             const CUtensorMap* ma = region == 0 ? &mA0 : (region == 1 ? &mA1 : &mA2);
-            tma_load_2d(sA(s, 0), ma, &bar_full[s], kb * BK, mb * BM);
+            tma_load_2d(sA(s, 0), ma, &bar_full[s], kb * KBE, mb * BM);
           } else {
-            tma_load_2d(sA(s, 0), &mA0, &bar_full[s], kb * BK, mb * BM);
+            tma_load_2d(sA(s, 0), &mA0, &bar_full[s], kb * KBE, mb * BM);
           }
-          if (C::NA == 2) tma_load_2d(sA(s, 1), &mA1, &bar_full[s], kb * BK, mb * BM);
-          tma_load_2d(sB(s, 0), &mB0, &bar_full[s], kb * BK, nb * BN);
-          if (C::NB == 2) tma_load_2d(sB(s, 1), &mB1, &bar_full[s], kb * BK, nb * BN);
+          if (C::NA == 2) tma_load_2d(sA(s, 1), &mA1, &bar_full[s], kb * KBE, mb * BM);
+          tma_load_2d(sB(s, 0), &mB0, &bar_full[s], kb * KBE, nb * BN);
+          if (C::NB == 2) tma_load_2d(sB(s, 1), &mB1, &bar_full[s], kb * KBE, nb * BN);
         }
       }
       // Drain: the last use of every stage must have landed before exit.
@@ -246,14 +259,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(BM, BN);
-      constexpr uint32_t idesc_half = idesc_f16_f32(BM, BN / 2);
+      constexpr uint32_t idesc = I8 ? idesc_i8_s32(BM, BN) : idesc_f16_f32(BM, BN);
+      constexpr uint32_t idesc_half = I8 ? idesc_i8_s32(BM, BN / 2) : idesc_f16_f32(BM, BN / 2);
       // K chunks of every tile go to the two TMEM buffers alternately, in
       // one sequence over all tiles of this CTA: chunk k lands in buffer k & 1
       // (its (k >> 1)-th use).  The epilogue keeps each tile's running total
       // in the buffer of its latest chunk (chunk_kb == 0: one chunk per tile,
       // plain double buffering across tiles).
-      uint32_t it = 0, k = 0;
+      uint32_t it = 0, kc = 0;  // k-blocks and chunks issued so far
       bool ok = true;
       const uint64_t dbase = desc_k_sw128(smem_u32(smem));
       const int chunk_len = a.chunk_kb > 0 ? a.chunk_kb : kblocks;
@@ -265,8 +278,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (first) left = chunk_len;
           const bool last = --left == 0 || kb + 1 == kblocks;
           if (first) {
-            b = k & 1;
-            if (!mbar_wait(&bar_acce[b], ((k >> 1) & 1) ^ 1, a.err, kErrWaitAccEmpty, &abort_flag)) {
+            b = kc & 1;
+            if (!mbar_wait(&bar_acce[b], ((kc >> 1) & 1) ^ 1, a.err, kErrWaitAccEmpty, &abort_flag)) {
               ok = false;
               break;
             }
@@ -283,14 +296,24 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint64_t ga = desc_add(dbase, s * C::STAGE_BYTES);   // A (hi) of stage s
           const uint64_t gb = desc_add(ga, C::NA * C::A_BYTES);       // B (hi) of stage s
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
+          for (int k = 0; k < 4; ++k) {  // 32 bytes of K per MMA: 16 fp16 or 32 int8 elements
             const uint64_t da0 = desc_add(ga, k * 32), db0 = desc_add(gb, k * 32);
             const uint32_t acc = (!first || k > 0) ? 1u : 0u;
             if (AMODE == 2) {
               // halves of the B tile (rows [0, BN/2) and [BN/2, BN)) against their own codes
-              mma_f16_ss(d, da0, db0, idesc_half, acc);
-              mma_f16_ss(d + BN / 2, desc_add(ga, C::A_BYTES + k * 32), desc_add(gb, (BN / 2) * 128 + k * 32),
-                         idesc_half, acc);
+              const uint64_t da1 = desc_add(ga, C::A_BYTES + k * 32), db1 = desc_add(gb, (BN / 2) * 128 + k * 32);
+              if (I8) {
+                mma_i8_ss(d, da0, db0, idesc_half, acc);
+                mma_i8_ss(d + BN / 2, da1, db1, idesc_half, acc);
+              } else {
+                mma_f16_ss(d, da0, db0, idesc_half, acc);
+                mma_f16_ss(d + BN / 2, da1, db1, idesc_half, acc);
+              }
+              continue;
+            }
+            if (I8) {
+              if (k == 0) mma_i8_ss(d, da0, db0, idesc, acc);
+              else mma_i8_ss_c<true>(d, da0, db0, idesc);
               continue;
             }
             if (k == 0) mma_f16_ss(d, da0, db0, idesc, acc);
@@ -301,7 +324,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           mma_commit(&bar_empty[s]);
           if (last) {
             mma_commit(&bar_accf[b]);
-            ++k;
+            ++kc;
             left = 0;
           }
         }
@@ -321,20 +344,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int eg = (warp - 2) >> 2;
     const int row_in_tile = 32 * q + lane;
     uint4* stage = reinterpret_cast<uint4*>(smem + C::STAGES * C::STAGE_BYTES + (warp - 2) * C::EPI_STAGE);
-    const int nchunks = a.chunk_kb ? (kblocks + a.chunk_kb - 1) / a.chunk_kb : 1;
+    const int nchunks = (!I8 && a.chunk_kb) ? (kblocks + a.chunk_kb - 1) / a.chunk_kb : 1;
     const uint32_t lq = (uint32_t)(32 * q) << 16;
-    uint32_t k = 0;  // chunks consumed so far (the MMA warp's sequence)
+    uint32_t kc = 0;  // chunks consumed so far (the MMA warp's sequence)
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
       // tcgen05.ld is warp-collective: every lane takes the same branch.
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[k & 1], (k >> 1) & 1, a.err, kErrWaitAccFull, &abort_flag));
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[kc & 1], (kc >> 1) & 1, a.err, kErrWaitAccFull, &abort_flag));
       if (!ok) break;
-      ++k;
+      ++kc;
       // Every later chunk of the tile: total (previous buffer) + chunk (its
       // buffer) with round-to-nearest f32 adds, written into the chunk's
       // buffer; the previous buffer is handed back as soon as it is read.
-      for (int c = 1; c < nchunks && ok; ++c, ++k) {
-        const uint32_t cb = k & 1, tb_ = cb ^ 1;
-        ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[cb], (k >> 1) & 1, a.err, kErrWaitAccFull, &abort_flag));
+      for (int c = 1; c < nchunks && ok; ++c, ++kc) {
+        const uint32_t cb = kc & 1, tb_ = cb ^ 1;
+        ok = __all_sync(0xffffffffu, mbar_wait(&bar_accf[cb], (kc >> 1) & 1, a.err, kErrWaitAccFull, &abort_flag));
         if (!ok) break;
         tc_fence_after();
         constexpr int COLS = BN / kEpiGroups;  // this warpgroup's columns
@@ -357,7 +380,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         tmem_wait_st_all();
       }
       if (!ok) break;
-      const uint32_t buf = (k - 1) & 1;  // the buffer holding the tile's total
+      const uint32_t buf = (kc - 1) & 1;  // the buffer holding the tile's total
       tc_fence_after();
       const int mb = tile / tiles_n, nb = tile % tiles_n;
       const uint32_t tb = tmem_base + ((uint32_t)(32 * q) << 16) + buf * BN;
@@ -372,7 +395,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
         for (int c = eg * NCH; c < (eg + 1) * NCH; ++c) {
           float v[32];
-          tmem_ld32(tb + c * 32, v);
+          acc_ld32<I8>(tb + c * 32, v);
           if (valid) {
             const int n0 = nb * BN + c * 32;
             if (EPI == EPI_PATCH) {
@@ -409,10 +432,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int n0 = nb * BN + c * 32;
           if (EPI == EPI_SILU) {
             char* bh_ = reinterpret_cast<char*>(a.out_hi + (size_t)wrow0 * a.ldh + n0);
-            if (a.s_code != 0.0f) {
-              uint4 w[4];
-              pack_codes(v, a.s_code, w);
-              warp_store_block<64>(stage, w, bh_, (size_t)a.ldh * 2, wrows, lane);
+            if (a.s_code != 0.0f) {  // signed-byte codes for the next GEMM (ldh bytes per row)
+              uint4 w[2];
+              pack_codes_i8(v, a.s_code, w);
+              warp_store_block<32>(stage, w, reinterpret_cast<char*>(a.out_hi) + (size_t)wrow0 * a.ldh + n0,
+                                   (size_t)a.ldh, wrows, lane);
             } else {
               uint4 w[4];
               pack_f16<false>(v, w, 4);
@@ -435,8 +459,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
         for (int c = eg * NP; c < (eg + 1) * NP; ++c) {
           float g[32], u[32];
-          tmem_ld32(tb + c * 32, g);
-          tmem_ld32(tb + BN / 2 + c * 32, u);
+          acc_ld32<I8>(tb + c * 32, g);
+          acc_ld32<I8>(tb + BN / 2 + c * 32, u);
           if (valid) {
             const int ng = nb * BN + c * 32, nu = nb * BN + BN / 2 + c * 32;
             float sg[32], su[32];
@@ -464,10 +488,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const int no = nb * (BN / 2) + c * 32;
           if (EPI == EPI_GELU_GATE) {
             char* bh_ = reinterpret_cast<char*>(a.out_hi + (size_t)wrow0 * a.ldh + no);
-            if (a.s_code != 0.0f) {
-              uint4 w[4];
-              pack_codes(g, a.s_code, w);
-              warp_store_block<64>(stage, w, bh_, (size_t)a.ldh * 2, wrows, lane);
+            if (a.s_code != 0.0f) {  // signed-byte codes for the next GEMM (ldh bytes per row)
+              uint4 w[2];
+              pack_codes_i8(g, a.s_code, w);
+              warp_store_block<32>(stage, w, reinterpret_cast<char*>(a.out_hi) + (size_t)wrow0 * a.ldh + no,
+                                   (size_t)a.ldh, wrows, lane);
             } else {
               uint4 w[4];
               pack_f16<false>(g, w, 4);
@@ -502,8 +527,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
           for (int hh = eg * NH; hh < (eg + 1) * NH; ++hh) {
             float v[64];
-            tmem_ld32(tb + hh * 64, v);
-            tmem_ld32(tb + hh * 64 + 32, v + 32);
+            acc_ld32<I8>(tb + hh * 64, v);
+            acc_ld32<I8>(tb + hh * 64 + 32, v + 32);
             if (valid) {
               qkv_head_norm(v, a.col_scale + n_tile0 + hh * 64, rsw, so, a.eps, nw);
               const float4* cs = reinterpret_cast<const float4*>(a.rope_cs) + (size_t)tok * 16;
@@ -548,8 +573,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll 1
           for (int hh = eg * NH; hh < (eg + 1) * NH; ++hh) {
             float v[64];
-            tmem_ld32(tb + hh * 64, v);
-            tmem_ld32(tb + hh * 64 + 32, v + 32);
+            acc_ld32<I8>(tb + hh * 64, v);
+            acc_ld32<I8>(tb + hh * 64 + 32, v + 32);
             if (!valid && !pair_v) continue;
             qkv_head_norm(v, a.col_scale + n_tile0 + hh * 64, rsw, so, a.eps, nullptr);
             const size_t bh = (size_t)img * a.heads + head0 + hh;
@@ -634,6 +659,20 @@ bool make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
   return r == CUDA_SUCCESS;
 }
 
+// int8 matrix [rows, cols] (row-major), box 128 columns x box_rows rows, 128B swizzle.
+bool make_tmap_i8(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || !base || (cols % 128) != 0 || (reinterpret_cast<uintptr_t>(base) % 16) != 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool make_tmap_f16_any(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                        uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -675,16 +714,20 @@ static cudaError_t launch_t(const GemmOperands& op, const GemmArgs& args, cudaSt
   }
   if (AMODE == 1 && (args.proj_width <= 0 || args.proj_width % BN != 0 || args.N > 3 * args.proj_width))
     return cudaErrorInvalidValue;  // every tile must sit inside one region
+  // one-term GEMMs read signed-byte codes and int8 weights; the rest fp16 planes
+  auto tmap = [](CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    return TERMS == 1 ? make_tmap_i8(m, base, rows, cols, box_rows) : make_tmap_f16(m, base, rows, cols, box_rows);
+  };
   CUtensorMap mA0, mA1, mA2, mB0, mB1;
-  if (!make_tmap_f16(&mA0, op.a_hi, args.M, args.K, BM)) return cudaErrorInvalidValue;
-  if (!make_tmap_f16(&mB0, op.b_hi, args.N, args.K, BN)) return cudaErrorInvalidValue;
+  if (!tmap(&mA0, op.a_hi, args.M, args.K, BM)) return cudaErrorInvalidValue;
+  if (!tmap(&mB0, op.b_hi, args.N, args.K, BN)) return cudaErrorInvalidValue;
   mA1 = mA0;
   mA2 = mA0;
   mB1 = mB0;
-  if ((C::NA == 2 || AMODE == 1) && !make_tmap_f16(&mA1, op.a_lo, args.M, args.K, BM)) return cudaErrorInvalidValue;
-  if (AMODE == 1 && args.N > 2 * args.proj_width && !make_tmap_f16(&mA2, op.a_c, args.M, args.K, BM))
+  if ((C::NA == 2 || AMODE == 1) && !tmap(&mA1, op.a_lo, args.M, args.K, BM)) return cudaErrorInvalidValue;
+  if (AMODE == 1 && args.N > 2 * args.proj_width && !tmap(&mA2, op.a_c, args.M, args.K, BM))
     return cudaErrorInvalidValue;
-  if (C::NB == 2 && !make_tmap_f16(&mB1, op.b_lo, args.N, args.K, BN)) return cudaErrorInvalidValue;
+  if (C::NB == 2 && !tmap(&mB1, op.b_lo, args.N, args.K, BN)) return cudaErrorInvalidValue;
   const int tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
   int grid = std::min(tiles, g_num_sms(dev));
   if (max_ctas > 0) grid = std::min(grid, max_ctas);
@@ -695,7 +738,7 @@ static cudaError_t launch_t(const GemmOperands& op, const GemmArgs& args, cudaSt
 
 cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, const GemmArgs& args_in, cudaStream_t st,
                         int max_ctas, int amode) {
-  if (args_in.K % BK != 0 || args_in.N % bn != 0 || args_in.M <= 0) return cudaErrorInvalidValue;
+  if (args_in.K % (terms == 1 ? BK_I8 : BK) != 0 || args_in.N % bn != 0 || args_in.M <= 0) return cudaErrorInvalidValue;
   GemmArgs args = args_in;
   if (terms == 1) args.chunk_kb = 0;  // integer codes: the products and their sums are exact integers
 #define G4M_CASE(BN_, T_, E_, A_) \
@@ -722,10 +765,10 @@ cudaError_t gemm_launch(int bn, int terms, int epi, const GemmOperands& op, cons
 // Operand preparation kernels
 // ---------------------------------------------------------------------------
 
-// x f32 [rows, cols] -> hi/lo fp16 planes.  s_in > 0 quantises first
-// (srqScalar) and stores the integer code k (exact in fp16, lo = 0); the
-// GEMM epilogue then scales by s_in.  row_scale (optional, [rows]) multiplies
-// x first (the embedder's inverse RMS).
+// x f32 [rows, cols] -> hi/lo fp16 planes.  s_in != 0 quantises instead
+// (srqScalar) and stores the integer code as a signed byte in `hi` (row
+// stride cols bytes) for the int8 GEMM, whose epilogue scales by s_in.
+// row_scale (optional, [rows]) multiplies x first (the embedder's inverse RMS).
 __global__ void prep_a_kernel(const float* __restrict__ x, long rows, int cols, float s_in, const float* row_scale,
                               __half* __restrict__ hi, __half* __restrict__ lo) {
   const long n = rows * (long)cols;
@@ -733,15 +776,14 @@ __global__ void prep_a_kernel(const float* __restrict__ x, long rows, int cols, 
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     float v = x[i];
     if (row_scale) v = v * row_scale[i / cols];
-    __half h, l;
     if (s_in != 0.0f) {
-      h = __float2half_rn(srq_code(v, s_in, inv_s));
-      l = __float2half_rn(0.0f);
+      reinterpret_cast<int8_t*>(hi)[i] = (int8_t)srq_code(v, s_in, inv_s);
     } else {
+      __half h, l;
       split_f16(v, h, l);
+      hi[i] = h;
+      lo[i] = l;
     }
-    hi[i] = h;
-    lo[i] = l;
   }
 }
 
@@ -798,6 +840,38 @@ cudaError_t prep_w(const void* src, int kind, int bits, int rows, int cols, cons
   int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
   if (grid <= 0) return cudaSuccess;
   prep_w_kernel<<<grid, 256, 0, st>>>(src, kind, bits, rows, cols, map, hi, lo);
+  return cudaGetLastError();
+}
+
+// Weight conversion to signed bytes for the int8 GEMMs (static input
+// quantisation).  dst_row = map ? map[r] : r.
+//   kind 0: int8 [rows, cols]                      value = w
+//   kind 1: unsigned codes packed `bits` per lane   value = code - 2^(bits-1)
+__global__ void prep_w_i8_kernel(const void* __restrict__ src, int kind, int bits, int rows, int cols, const int* map,
+                                 int8_t* __restrict__ dst) {
+  const long n = (long)rows * cols;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    int v;
+    if (kind == 0) {
+      v = reinterpret_cast<const int8_t*>(src)[i];
+    } else {
+      const uint8_t* w = reinterpret_cast<const uint8_t*>(src);
+      const int vpb = 8 / bits;
+      const long bpr = (long)cols * bits / 8;
+      const uint8_t byte = w[(long)r * bpr + c / vpb];
+      v = ((byte >> ((c % vpb) * bits)) & ((1 << bits) - 1)) - (1 << (bits - 1));
+    }
+    dst[(long)(map ? map[r] : r) * cols + c] = (int8_t)v;
+  }
+}
+
+cudaError_t prep_w_i8(const void* src, int kind, int bits, int rows, int cols, const int* map, int8_t* dst,
+                      cudaStream_t st) {
+  const long n = (long)rows * cols;
+  int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
+  if (grid <= 0) return cudaSuccess;
+  prep_w_i8_kernel<<<grid, 256, 0, st>>>(src, kind, bits, rows, cols, map, dst);
   return cudaGetLastError();
 }
 

@@ -456,8 +456,22 @@ __global__ void __launch_bounds__(128, 4) audio_attn_kernel(const float* __restr
         if (qi < nq) {
           const int wd = qi * 16 + 4 * (c ^ ((qi >> 1) & 3));
           const long oi = (r0 + b * CH + qi) * D + head * HD + warp * 32 + c * 8;
-          *reinterpret_cast<uint4*>(o_hi + oi) = *reinterpret_cast<const uint4*>(sth + wd);
-          if (s_code == 0.0f) *reinterpret_cast<uint4*>(o_lo + oi) = *reinterpret_cast<const uint4*>(stl + wd);
+          if (s_code != 0.0f) {
+            // the staged codes (small integers, exact in fp16) leave as signed
+            // bytes: 8 per lane, D bytes per row
+            const uint4 hw = *reinterpret_cast<const uint4*>(sth + wd);
+            const uint32_t src[4] = {hw.x, hw.y, hw.z, hw.w};
+            uint32_t by[2] = {0, 0};
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const __half hv = __ushort_as_half((unsigned short)(src[e >> 1] >> (16 * (e & 1))));
+              by[e >> 2] |= ((uint32_t)(int)__half2float(hv) & 0xFFu) << (8 * (e & 3));
+            }
+            *reinterpret_cast<uint2*>(reinterpret_cast<char*>(o_hi) + oi) = make_uint2(by[0], by[1]);
+          } else {
+            *reinterpret_cast<uint4*>(o_hi + oi) = *reinterpret_cast<const uint4*>(sth + wd);
+            *reinterpret_cast<uint4*>(o_lo + oi) = *reinterpret_cast<const uint4*>(stl + wd);
+          }
         }
       }
     }
@@ -599,15 +613,20 @@ __global__ void __launch_bounds__(256, 2) lconv_kernel(const float* __restrict__
           const float4 x = xr[lane + 32 * v];
           float u4[4] = {(x.x * inv) * nv[v].x, (x.y * inv) * nv[v].y, (x.z * inv) * nv[v].z, (x.w * inv) * nv[v].w};
           __align__(8) __half hh[4], ll[4];
+          uint32_t codes = 0;  // signed-byte codes for linear_end's input scale (D bytes per row)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const float sv = u4[u] * sigmoid_f(u4[u]);
-            if (s_code != 0.0f) hh[u] = __float2half_rn(srq_code(sv, s_code, inv_code));
+            if (s_code != 0.0f) codes |= ((uint32_t)(int)srq_code(sv, s_code, inv_code) & 0xFFu) << (8 * u);
             else split_f16(sv, hh[u], ll[u]);
           }
           const int c = 4 * (lane + 32 * v);
-          *reinterpret_cast<uint2*>(a_hi + row * D + c) = *reinterpret_cast<uint2*>(hh);
-          if (s_code == 0.0f) *reinterpret_cast<uint2*>(a_lo + row * D + c) = *reinterpret_cast<uint2*>(ll);
+          if (s_code != 0.0f) {
+            *reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(a_hi) + row * D + c) = codes;
+          } else {
+            *reinterpret_cast<uint2*>(a_hi + row * D + c) = *reinterpret_cast<uint2*>(hh);
+            *reinterpret_cast<uint2*>(a_lo + row * D + c) = *reinterpret_cast<uint2*>(ll);
+          }
         }
       }
     }

@@ -78,9 +78,6 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(RowArgs r) {
   if (r.w_next) {
     const float inv = inv_rms<V>(h, d, r.eps);
     const float4* w = reinterpret_cast<const float4*>(r.w_next);
-    __half* ah = r.a_hi + row * r.lda;
-    __half* al = r.a_lo + row * r.lda;
-    __half* ac = r.a_c ? r.a_c + row * r.lda : nullptr;
     const float inv_a = r.s_in_next != 0.0f ? 1.0f / r.s_in_next : 0.0f;
     const float inv_b = r.s_in_b != 0.0f ? 1.0f / r.s_in_b : 0.0f;
     const float inv_c = r.s_in_c != 0.0f ? 1.0f / r.s_in_c : 0.0f;
@@ -88,23 +85,28 @@ __global__ void __launch_bounds__(256) fused_rows_kernel(RowArgs r) {
     for (int i = 0; i < V; ++i) {
       const float4 wv = w[lane + 32 * i];
       float v[4] = {(h[i].x * inv) * wv.x, (h[i].y * inv) * wv.y, (h[i].z * inv) * wv.z, (h[i].w * inv) * wv.w};
-      __align__(8) __half hh[4], ll[4], cc[4];
       const int c = 4 * (lane + 32 * i);
       if (r.s_in_next != 0.0f) {
-        // integer codes per consumer scale: a_hi (s_in_next), a_lo (s_in_b), a_c (s_in_c)
+        // integer codes per consumer scale as signed bytes (lda bytes per row):
+        // a_hi (s_in_next), a_lo (s_in_b), a_c (s_in_c)
+        uint32_t ca = 0, cb = 0, cc = 0;
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          hh[u] = __float2half_rn(srq_code(v[u], r.s_in_next, inv_a));
-          ll[u] = __float2half_rn(r.s_in_b != 0.0f ? srq_code(v[u], r.s_in_b, inv_b) : 0.0f);
-          if (ac) cc[u] = __float2half_rn(srq_code(v[u], r.s_in_c, inv_c));
+          ca |= ((uint32_t)(int)srq_code(v[u], r.s_in_next, inv_a) & 0xFFu) << (8 * u);
+          if (r.s_in_b != 0.0f) cb |= ((uint32_t)(int)srq_code(v[u], r.s_in_b, inv_b) & 0xFFu) << (8 * u);
+          if (r.a_c) cc |= ((uint32_t)(int)srq_code(v[u], r.s_in_c, inv_c) & 0xFFu) << (8 * u);
         }
-        if (ac) *reinterpret_cast<uint2*>(ac + c) = *reinterpret_cast<uint2*>(cc);
+        const long o = row * r.lda + c;
+        *reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(r.a_hi) + o) = ca;
+        if (r.s_in_b != 0.0f) *reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(r.a_lo) + o) = cb;
+        if (r.a_c) *reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(r.a_c) + o) = cc;
       } else {
+        __align__(8) __half hh[4], ll[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) split_f16(v[u], hh[u], ll[u]);
+        *reinterpret_cast<uint2*>(r.a_hi + row * r.lda + c) = *reinterpret_cast<uint2*>(hh);
+        *reinterpret_cast<uint2*>(r.a_lo + row * r.lda + c) = *reinterpret_cast<uint2*>(ll);
       }
-      *reinterpret_cast<uint2*>(ah + c) = *reinterpret_cast<uint2*>(hh);
-      *reinterpret_cast<uint2*>(al + c) = *reinterpret_cast<uint2*>(ll);
     }
   }
 }

@@ -194,10 +194,11 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const __half* __restrict
   const float inv = 1.0f / l;
   __half* dh = oh + orow * (size_t)(heads * 64) + head * 64;
   __half* dl = ol + orow * (size_t)(heads * 64) + head * 64;
+  int8_t* dc = reinterpret_cast<int8_t*>(oh) + orow * (size_t)(heads * 64) + head * 64;
 #pragma unroll
   for (int d = 0; d < 64; ++d) {
-    if (s_code != 0.0f) {  // integer codes for the o_proj input scale
-      dh[d] = __float2half_rn(srq_code(o[d] * inv, s_code, 1.0f / s_code));
+    if (s_code != 0.0f) {  // signed-byte codes for the o_proj input scale
+      dc[d] = (int8_t)srq_code(o[d] * inv, s_code, 1.0f / s_code);
     } else {
       __half h, lo;
       split_f16(o[d] * inv, h, lo);

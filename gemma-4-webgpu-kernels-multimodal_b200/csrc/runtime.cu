@@ -184,8 +184,13 @@ int load_qat(Device& d, const SafeTensors& f, const std::string& prefix, const s
   if (cudaMemcpy(staging.p, f.data(*w), f.bytes(*w), cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemcpy(map_dev.p, map.data(), map.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess)
     return fail(G4M_E_CUDA, "weight upload failed");
-  if (prep_w(staging.p, packed ? 1 : 0, bits, out, in, (const int*)map_dev.p, dst, nullptr, 0) != cudaSuccess)
-    return fail(G4M_E_CUDA, "weight conversion launch failed");
+  // statically quantised inputs (s_in != 0) run on the int8 GEMM: the weights
+  // are stored as signed bytes (rows of `in` bytes) in the same buffer
+  const cudaError_t ce = s_in != 0.0f
+                             ? prep_w_i8(staging.p, packed ? 1 : 0, bits, out, in, (const int*)map_dev.p,
+                                         reinterpret_cast<int8_t*>(dst), 0)
+                             : prep_w(staging.p, packed ? 1 : 0, bits, out, in, (const int*)map_dev.p, dst, nullptr, 0);
+  if (ce != cudaSuccess) return fail(G4M_E_CUDA, "weight conversion launch failed");
   if (cudaDeviceSynchronize() != cudaSuccess) return fail(G4M_E_CUDA, "weight conversion failed");
   return G4M_OK;
 }
@@ -639,7 +644,11 @@ int qat_linear_device(Device& d, const __half* w16, const float* scale, const fl
   return G4M_OK;
 }
 
-bool qat_tensor_core_shape(int in, int out) { return in % 64 == 0 && out % 256 == 0; }
+// The tensor-core GEMMs take K in 64-element (fp16) or 128-element (int8)
+// blocks and N in 256-column tiles; other shapes use the SIMT kernel.
+bool qat_tensor_core_shape(int in, int out, float s_in) {
+  return in % (s_in != 0.0f ? 128 : 64) == 0 && out % 256 == 0;
+}
 
 }  // namespace g4m
 
@@ -755,7 +764,7 @@ int g4m_qat_linear(g4m_ctx* ctx, int di, const float* x, int rows, int in, int o
   // every call; the device buffers persist across calls (grown on demand),
   // everything runs on the device's stream, and the host waits once.
   const size_t wbytes = bits ? (size_t)out * in * bits / 8 : (size_t)out * in;
-  const bool tc = qat_tensor_core_shape(in, out);
+  const bool tc = qat_tensor_core_shape(in, out, s_in);
   if (ensure(d.qw_raw, wbytes) || ensure(d.qscale, (size_t)out * 4) || (bias && ensure(d.qbias, (size_t)out * 4)) ||
       ensure(d.qx, (size_t)rows * in * 4) || ensure(d.qy, (size_t)rows * out * 4) ||
       (tc && ensure(d.qw16, (size_t)out * in * 2)))
@@ -766,7 +775,10 @@ int g4m_qat_linear(g4m_ctx* ctx, int di, const float* x, int rows, int in, int o
       (bias && cudaMemcpyAsync(d.qbias.p, bias, (size_t)out * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) ||
       cudaMemcpyAsync(d.qx.p, x, (size_t)rows * in * 4, cudaMemcpyHostToDevice, st) != cudaSuccess)
     return fail(G4M_E_CUDA, "QAT linear upload failed");
-  if (tc) G4M_RUN("prep_w", prep_w(d.qw_raw.p, bits ? 1 : 0, bits, out, in, nullptr, (__half*)d.qw16.p, nullptr, st));
+  if (tc && s_in != 0.0f)
+    G4M_RUN("prep_w", prep_w_i8(d.qw_raw.p, bits ? 1 : 0, bits, out, in, nullptr, (int8_t*)d.qw16.p, st));
+  else if (tc)
+    G4M_RUN("prep_w", prep_w(d.qw_raw.p, bits ? 1 : 0, bits, out, in, nullptr, (__half*)d.qw16.p, nullptr, st));
   int rc = qat_linear_device(d, tc ? (const __half*)d.qw16.p : nullptr, (const float*)d.qscale.p,
                              bias ? (const float*)d.qbias.p : nullptr, d.qw_raw.p, bits, rows, in, out, s_in, s_out,
                              (const float*)d.qx.p, (float*)d.qy.p, d.qa_hi, d.qa_lo, st);
@@ -798,9 +810,11 @@ int g4m_linear_prepare(g4m_ctx* ctx, int di, const void* w, int bits, int out, i
   if (ok && bias)
     ok = cudaMalloc(&L->bias, (size_t)out * 4) == cudaSuccess &&
          cudaMemcpy(L->bias, bias, (size_t)out * 4, cudaMemcpyHostToDevice) == cudaSuccess;
-  if (ok && qat_tensor_core_shape(in, out)) {
+  if (ok && qat_tensor_core_shape(in, out, s_in)) {
+    // fp16 weights for the split-operand GEMM, or signed bytes for the int8 GEMM (s_in != 0)
     ok = cudaMalloc(&L->w16, (size_t)out * in * 2) == cudaSuccess &&
-         prep_w(L->w_raw, bits ? 1 : 0, bits, out, in, nullptr, L->w16, nullptr, 0) == cudaSuccess &&
+         (s_in != 0.0f ? prep_w_i8(L->w_raw, bits ? 1 : 0, bits, out, in, nullptr, reinterpret_cast<int8_t*>(L->w16), 0)
+                       : prep_w(L->w_raw, bits ? 1 : 0, bits, out, in, nullptr, L->w16, nullptr, 0)) == cudaSuccess &&
          cudaDeviceSynchronize() == cudaSuccess;
   }
   if (!ok) {
