@@ -104,51 +104,78 @@ def weights_path(tower: str, layers: int, quant: str, rank: int, barrier) -> str
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
-    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-              "clocks_event_reasons.sw_power_cap")
+    """nvidia-smi clock / throttle-reason sampling.  nvidia-smi runs for the
+    whole process at a 50 ms period with timestamps; only samples that fall
+    inside the timed windows (window() around each timed region) count."""
+    FIELDS = ("timestamp,uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    PERIOD_MS = 50
 
     def __init__(self, uuid: str, index: int):
         self.uuid = uuid.lower().replace("gpu-", "")
         self.index = index
-        self.rows = []
         self.all = []
+        self.windows = []
         self.proc = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                          "-lms", str(self.PERIOD_MS)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
         except Exception:
             self.proc = None
 
     def _read(self):
+        import datetime
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.all.append(parts)
-                if self.uuid and self.uuid in parts[0].lower():
-                    self.rows.append(parts)
+            if len(parts) >= 10:
+                try:
+                    t = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                self.all.append([t] + parts[1:])
+
+    class _Window:
+        def __init__(self, owner):
+            self.owner = owner
+
+        def __enter__(self):
+            self.t0 = time.time()
+
+        def __exit__(self, *exc):
+            self.owner.windows.append((self.t0, time.time()))
+            return False
+
+    def window(self):
+        """Context manager marking one timed region."""
+        return ClockSampler._Window(self)
 
     def stop(self):
         if self.proc:
+            time.sleep(2 * self.PERIOD_MS / 1000.0)  # the samples of the last window's end
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-        if not self.rows and self.all:  # UUID formats differ: fall back to the device ordinal
-            uuids = sorted({r[0] for r in self.all})
+        mine = [r for r in self.all if self.uuid and self.uuid in r[1].lower()]
+        if not mine and self.all:  # UUID formats differ: fall back to the device ordinal
+            uuids = sorted({r[1] for r in self.all})
             pick = uuids[self.index] if self.index < len(uuids) else uuids[0]
-            self.rows = [r for r in self.all if r[0] == pick]
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+            mine = [r for r in self.all if r[1] == pick]
+        slack = self.PERIOD_MS / 1000.0
+        rows = [r for r in mine if any(t0 - slack <= r[0] <= t1 + slack for t0, t1 in self.windows)]
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        mx = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4) if "Active" in r[5 + i] and "Not" not in r[5 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[6 + i] and "Not" not in r[6 + i]})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(rows), "timed_windows": len(self.windows),
+                "timed_s": round(sum(t1 - t0 for t0, t1 in self.windows), 3)}
 
 
 def measured_peaks():
@@ -348,7 +375,7 @@ def timed_steps(step, stream, steps: int, flush):
     return sum(a.elapsed_time(b) for a, b in evs)
 
 
-def run_audio(args, native, syn, rank, world, dist, barrier, flush):
+def run_audio(args, native, syn, rank, world, dist, barrier, flush, clocks):
     """Batched audio: the job's clips, lengths U[1, 30] s, packed without
     padding rows, this rank's LPT share.  Returns the sub-object of the JSON
     line (rank 0)."""
@@ -380,7 +407,8 @@ def run_audio(args, native, syn, rank, world, dist, barrier, flush):
     torch.cuda.synchronize()
     barrier()
     launches0 = native.kernel_launches()
-    ms = timed_steps(step, stream, args.steps, flush)
+    with clocks.window():
+        ms = timed_steps(step, stream, args.steps, flush)
     launches = native.kernel_launches() - launches0
     ms = sharding.max_over_ranks(ms, dist, "cuda")
     value = job_seconds * args.steps / (ms / 1000.0)
@@ -578,18 +606,18 @@ def run_ours(args):
     def step():
         ctx.vision_embed_device(pix.data_ptr(), B, H, Wd, out.data_ptr(), max_soft, layers, stream.cuda_stream)
 
+    clocks = ClockSampler(str(torch.cuda.get_device_properties(local).uuid), local)
+    clocks.start()
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             step()
     torch.cuda.synchronize()
     barrier()
-    clocks = ClockSampler(str(torch.cuda.get_device_properties(local).uuid), local)
-    clocks.start()
     launches0 = native.kernel_launches()
-    ms = timed_steps(step, stream, args.steps, flush)
+    with clocks.window():
+        ms = timed_steps(step, stream, args.steps, flush)
     launches = native.kernel_launches() - launches0
     barrier()
-    clk = clocks.stop()
     ms_max = sharding.max_over_ranks(ms, dist, "cuda")
     value = n_job * args.steps / (ms_max / 1000.0)
 
@@ -654,7 +682,8 @@ def run_ours(args):
     audio = None
     if not args.no_audio:
         ctx.close()
-        audio = run_audio(args, native, syn, rank, world, dist, barrier, flush)
+        audio = run_audio(args, native, syn, rank, world, dist, barrier, flush, clocks)
+    clk = clocks.stop()
 
     if rank == 0:
         line = {
@@ -675,7 +704,7 @@ def run_ours(args):
             "qat_cfg0": cfg0,
             "kernel_ms_per_step": kernel_ms,
             "cpu_baseline": cpu,
-            "clocks": clk,
+            "clocks": clk,  # samples inside the timed windows of both towers
         }
         if audio:
             line["audio"] = audio
