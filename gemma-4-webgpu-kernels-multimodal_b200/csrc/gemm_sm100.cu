@@ -13,12 +13,18 @@
 // accumulation in tensor memory.  Activations are carried as two fp16
 // planes (hi = fp16(x), lo = fp16(x - hi)), so one QAT linear is
 // hi*W + lo*W (int8 / unsigned-code weights are exact in fp16) and an F32
-// linear adds hi*W_lo: fp32-grade results from the fp16 tensor path.
+// linear adds hi*W_lo: fp32-grade results from the fp16 tensor path.  The
+// tensor core truncates each product to the running accumulator's precision,
+// so callers can split K into chunks (GemmArgs::chunk_kb) that are summed
+// with round-to-nearest f32 adds.  One-term GEMMs run on statically
+// quantised inputs: signed-byte codes x int8 weights, tcgen05 kind::i8,
+// exact int32 accumulation.
 //
 // Kernel structure (one CTA per SM, persistent over output tiles):
 //   warp 0       TMA producer (one elected lane), STAGES-deep smem ring
 //   warp 1       TMEM owner + MMA issuer (one lane), 2 accumulator buffers
-//   warps 2..5   epilogue: TMEM -> registers -> fused math -> global
+//   warps 2..9   two epilogue warpgroups (column halves of each tile):
+//                TMEM -> registers -> fused math -> global
 // Every wait is bounded; a timeout records an error word and the CTA
 // unwinds, drains its own in-flight copies and frees its TMEM.
 #include "g4m_kernels.h"
