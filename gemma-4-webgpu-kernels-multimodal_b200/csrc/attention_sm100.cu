@@ -7,12 +7,13 @@
 //
 // Operands are fp16 hi/lo planes, so every product is split into three
 // tensor-core terms (hi*hi + hi*lo + lo*hi) for fp32-grade scores and
-// outputs:   S = Qh Kh^T + Qh Kl^T + Ql Kh^T,   O += (Ph + Pl) (Vh + Vl).
+// outputs:   S = Qh Kh^T + Qh Kl^T + Ql Kh^T,   O += Ph (Vh + Vl) + Pl Vh.
 // An N = 64 tcgen05.mma takes three quarters of the time of an N = 128 one
 // (measured: 48 against 64 cycles), so P*V stacks the V hi and lo planes into
-// one N = 128 operand: Ph [Vh | Vl] and Pl [Vh | Vl] accumulate into 128 TMEM
-// columns whose two halves are summed at the end (two instructions per 16
-// keys instead of three N = 64 ones).
+// one N = 128 operand: Ph [Vh | Vl] (N = 128) and Pl Vh (N = 64, the stacked
+// operand's first 64 rows) accumulate into 128 TMEM columns whose two halves
+// are summed at the end (112 cycles per 16 keys, against 128 for
+// Pl [Vh | Vl] and 144 for three N = 64 products).
 //
 // One CTA per (image*head, 256 queries) = two 128-query tiles A and B that
 // share every K / V tile, 320 threads:
@@ -208,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16_f32(128, KT);
       constexpr uint32_t id_pv = idesc_f16_f32(128, 2 * HD);
+      constexpr uint32_t id_pv_h = idesc_f16_f32(128, HD);  // Pl Vh: the stacked operand's first 64 rows
       bool ok = mbar_wait(&b_q, 0, err, kErrWaitFull, &abort_flag);
       // Descriptor of the tile at byte offset 0 of the aligned region; every
       // operand descriptor below is this plus a constant offset.
@@ -232,21 +234,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&b_s[t]);
         return true;
       };
-      // O_t += P_t(j) V_j with P_t in TMEM: keys [16 kk, 16 kk + 16) hi at S column
-      // 32 (kk / 2) + 8 (kk % 2), lo 16 columns further
+      // O_t += Ph_t(j) [Vh | Vl]_j + Pl_t(j) Vh_j with P_t in TMEM: keys [16 kk, 16 kk + 16)
+      // hi at S column 32 (kk / 2) + 8 (kk % 2), lo 16 columns further
       auto issue_pv = [&](int t, int j) -> bool {
         if (!mbar_wait(&b_p[t], j & 1, err, kErrWaitFull, &abort_flag)) return false;
         tc_fence_after();
         const uint64_t v = desc_add(dbase, KV_OFF + (j & 1) * KV_STAGE + 2 * TILE_BYTES);
         const uint32_t d = tmem + O_COL + t * 2 * HD, a = tmem + t * KT;
         mma_f16_ts(d, a, v, id_pv, j > 0 ? 1u : 0u);  // the first product of the tile starts O at j = 0
-        mma_f16_ts_c<true>(d, a + 16, v, id_pv);
+        mma_f16_ts_c<true>(d, a + 16, v, id_pv_h);
 #pragma unroll
         for (int kk = 1; kk < KT / 16; ++kk) {
           const uint64_t dv = desc_add(v, (kk >> 2) * TILE_BYTES + (kk & 3) * 32);
           const uint32_t ah = a + 32 * (kk >> 1) + 8 * (kk & 1);
           mma_f16_ts_c<true>(d, ah, dv, id_pv);
-          mma_f16_ts_c<true>(d, ah + 16, dv, id_pv);
+          mma_f16_ts_c<true>(d, ah + 16, dv, id_pv_h);
         }
         mma_commit(&b_pv[t]);
         return true;
