@@ -78,7 +78,9 @@ __device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity, int
 // G_kl = (1 or 2)/128 sum_c w[c][k] w[c][l] (w0stat: 9 + 45 doubles), so
 // one thread per task computes them in double (54 FMAs) before the channel
 // pass.  The channel pass is one warp per task, lane = channels 4 lane ..
-// 4 lane + 3 (weights in registers), writing 256 contiguous bytes per plane.
+// 4 lane + 3 (weights in registers), writing 256 contiguous bytes per plane;
+// it applies the statistics in f32, (v - mean) (inv n_c) (v is the f32
+// 9-tap sum), so each value costs 9 FMAs and 3 more operations.
 __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restrict__ feats, const int* __restrict__ foff,
                                                            const int* __restrict__ fcount, const int* __restrict__ t0off,
                                                            const float* __restrict__ w0,
@@ -134,12 +136,13 @@ __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restri
     }
   }
   const float4 nq = __ldg(reinterpret_cast<const float4*>(n0) + lane);
-  const double nw[4] = {(double)nq.x, (double)nq.y, (double)nq.z, (double)nq.w};
+  const float nw[4] = {nq.x, nq.y, nq.z, nq.w};
+  const long row_c = (long)t0off[clip];
   __syncthreads();
   for (int task = warp; task < 256; task += 8) {
     const int rr = task >> 6, f0 = task & 63, r = rb + rr;
     if (r > T0) break;  // tasks run in row order
-    const long row = (long)t0off[clip] + r;
+    const long row = row_c + r;
     const long o = row * L0_ROW + f0 * 128 + 4 * lane;
     if (r == T0) {  // the zero row after the clip (and, for clip 0, the one before it)
       *reinterpret_cast<uint2*>(l0h + o) = make_uint2(0u, 0u);
@@ -159,15 +162,16 @@ __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restri
         const int sf = 2 * f0 + kf - 1;
         x[kt * 3 + kf] = sf >= 0 ? xs[2 * rr + kt][sf] : 0.f;
       }
+    // the statistics (double) applied in f32: (v - mean) (inv n_c), then ReLU
     const double2 s2 = mi[task];
+    const float mean_f = (float)s2.x, inv_f = (float)s2.y;
     float y[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       float v = 0.f;
 #pragma unroll
       for (int k = 0; k < 9; ++k) v = fmaf(x[k], w[j][k], v);
-      const double yd = ((double)v - s2.x) * s2.y * nw[j];
-      y[j] = yd > 0.0 ? (float)yd : 0.f;
+      y[j] = fmaxf((v - mean_f) * (inv_f * nw[j]), 0.f);
     }
     uint32_t h01, l01, h23, l23;
     split2_f16(y[0], y[1], h01, l01);
