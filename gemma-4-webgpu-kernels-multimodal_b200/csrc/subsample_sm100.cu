@@ -59,6 +59,14 @@ __device__ __forceinline__ double rsqrt_nr(double a) {
   return r;
 }
 
+__device__ __forceinline__ void mma_16816_s(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity, int* err) {
   const uint32_t b = smem_u32(bar);
   const long long t0 = clock64();
@@ -71,25 +79,38 @@ __device__ __forceinline__ void drain_wait_s(uint64_t* bar, uint32_t parity, int
 }
 }  // namespace
 
-// Layer 0 for 4 layer-0 rows x 64 frequencies per CTA (256 (row, frequency)
-// tasks).  The LayerNorm statistics of a task follow from its nine taps x_k:
-// with v_c = sum_k x_k w[c][k], mean = sum_k x_k wbar_k and
+// Layer 0 for 4 layer-0 rows x 64 frequencies per CTA (256 positions).  The
+// LayerNorm statistics of a position follow from its nine taps x_k: with
+// v_c = sum_k x_k w[c][k], mean = sum_k x_k wbar_k and
 // E[v^2] = sum_{k<=l} x_k x_l G_kl, where wbar_k = (1/128) sum_c w[c][k] and
 // G_kl = (1 or 2)/128 sum_c w[c][k] w[c][l] (w0stat: 9 + 45 doubles), so
-// one thread per task computes them in double (54 FMAs) before the channel
-// pass.  The channel pass is one warp per task, lane = channels 4 lane ..
-// 4 lane + 3 (weights in registers), writing 256 contiguous bytes per plane;
-// it applies the statistics in f32, (v - mean) (inv n_c) (v is the f32
-// 9-tap sum), so each value costs 9 FMAs and 3 more operations.
+// one thread per position computes them in double (54 FMAs).  The 128
+// channel values v_c of 16 positions are one mma.sync m16n8k16 product per
+// 8 channels: A = the positions' taps (K = 9, padded to 16), B = the filters,
+// both split as hi = f16(x), lo = f16((x - hi) 2^11), three products
+// (hi hi into one accumulator, hi lo + lo hi into another, scaled back by
+// 2^-11), i.e. the f32-grade 9-term sum.  Warp w takes row w / 2 and 32
+// frequencies (two 16-position tiles), four 8-channel tiles at a time; the
+// epilogue applies the statistics in f32, (v - mean) (inv n_c), then ReLU
+// and the hi / lo planes; each 32-channel chunk passes through the warp's
+// 2 KB staging block (16-byte pieces XOR-swizzled by position pair, both
+// phases free of bank conflicts) and leaves as 64 contiguous bytes per
+// position and plane.
 __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restrict__ feats, const int* __restrict__ foff,
                                                            const int* __restrict__ fcount, const int* __restrict__ t0off,
                                                            const float* __restrict__ w0,
                                                            const double* __restrict__ w0stat,
                                                            const float* __restrict__ n0, float eps,
                                                            __half* __restrict__ l0h, __half* __restrict__ l0l) {
-  __shared__ __align__(16) float xs[9][128];  // input frames 2 rb - 1 .. 2 rb + 7
+  constexpr int XP = 130;  // frames: column 0 is frequency -1 (zero), column f + 1 frequency f
+  constexpr int KP = 24;   // halves per filter row (taps 9..23 zero; 48-byte rows: B loads hit distinct banks)
+  constexpr float kS = 2048.0f;
+  __shared__ __align__(16) float xs[9][XP];  // input frames 2 rb - 1 .. 2 rb + 7
+  __shared__ __align__(16) __half wsh[128 * KP], wsl[128 * KP];
+  __shared__ __align__(16) float nsm[128];
   __shared__ double stat_s[54];
-  __shared__ __align__(16) double2 mi[256];    // (mean, 1 / sqrt(var + eps)) per task
+  __shared__ __align__(16) float2 mi[256];  // (mean, 1 / sqrt(var + eps)) per position, f32
+  __shared__ __align__(16) uint32_t stage[8 * 512];  // per warp: [16 positions][32 channels] hi, then lo
   const int clip = blockIdx.y, rb = blockIdx.x * 4;  // first layer-0 row of this CTA
   const int F = fcount[clip];
   const int T0 = (F - 1) / 2 + 1;
@@ -98,20 +119,26 @@ __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restri
   const float* fx = feats + (long)foff[clip] * 128;
   for (int i = t; i < 9 * 128; i += 256) {
     const int fr = 2 * rb - 1 + i / 128;
-    xs[i / 128][i % 128] = (fr >= 0 && fr < F) ? fx[(long)fr * 128 + (i % 128)] : 0.f;
+    xs[i / 128][1 + i % 128] = (fr >= 0 && fr < F) ? fx[(long)fr * 128 + (i % 128)] : 0.f;
   }
+  if (t < 9) xs[t][0] = 0.f;
+  for (int i = t; i < 128 * 16; i += 256) {
+    const int c = i >> 4, k = i & 15;
+    const float v = k < 9 ? __ldg(w0 + c * 9 + k) : 0.f;
+    const __half h = __float2half_rn(v);
+    wsh[c * KP + k] = h;
+    wsl[c * KP + k] = __float2half_rn((v - __half2float(h)) * kS);
+  }
+  if (t < 128) nsm[t] = __ldg(n0 + t);
   if (t < 54) stat_s[t] = w0stat[t];
   __syncthreads();
-  {  // statistics of task t = (row rb + t / 64, frequency t % 64)
+  {  // statistics of position t = (row rb + t / 64, frequency t % 64)
     const int rr = t >> 6, f0 = t & 63;
     double x[9];
 #pragma unroll
     for (int kt = 0; kt < 3; ++kt)
 #pragma unroll
-      for (int kf = 0; kf < 3; ++kf) {
-        const int sf = 2 * f0 + kf - 1;  // <= 127
-        x[kt * 3 + kf] = sf >= 0 ? (double)xs[2 * rr + kt][sf] : 0.0;
-      }
+      for (int kf = 0; kf < 3; ++kf) x[kt * 3 + kf] = (double)xs[2 * rr + kt][2 * f0 + kf];
     double mean = 0.0, e2 = 0.0;
     int q = 9;
 #pragma unroll
@@ -121,63 +148,100 @@ __global__ void __launch_bounds__(256) subsample_l0_kernel(const float* __restri
       for (int l = k; l < 9; ++l) e2 = fma(x[k] * x[l], stat_s[q++], e2);
     }
     const double var = fmax(e2 - mean * mean, 0.0);
-    mi[t] = make_double2(mean, rsqrt_nr(var + (double)eps));
+    mi[t] = make_float2((float)mean, (float)rsqrt_nr(var + (double)eps));
   }
-  float w[4][9];  // this lane's channels 4 lane .. 4 lane + 3: 9 float4 of w0 [128][9]
-  {
-    const float4* wv = reinterpret_cast<const float4*>(w0 + 36 * lane);
-#pragma unroll
-    for (int i = 0; i < 9; ++i) {
-      const float4 q4 = __ldg(wv + i);
-      w[(4 * i) / 9][(4 * i) % 9] = q4.x;
-      w[(4 * i + 1) / 9][(4 * i + 1) % 9] = q4.y;
-      w[(4 * i + 2) / 9][(4 * i + 2) % 9] = q4.z;
-      w[(4 * i + 3) / 9][(4 * i + 3) % 9] = q4.w;
-    }
-  }
-  const float4 nq = __ldg(reinterpret_cast<const float4*>(n0) + lane);
-  const float nw[4] = {nq.x, nq.y, nq.z, nq.w};
-  const long row_c = (long)t0off[clip];
   __syncthreads();
-  for (int task = warp; task < 256; task += 8) {
-    const int rr = task >> 6, f0 = task & 63, r = rb + rr;
-    if (r > T0) break;  // tasks run in row order
-    const long row = row_c + r;
-    const long o = row * L0_ROW + f0 * 128 + 4 * lane;
-    if (r == T0) {  // the zero row after the clip (and, for clip 0, the one before it)
-      *reinterpret_cast<uint2*>(l0h + o) = make_uint2(0u, 0u);
-      *reinterpret_cast<uint2*>(l0l + o) = make_uint2(0u, 0u);
-      if (clip == 0) {
-        const long o0 = (long)(t0off[0] - 1) * L0_ROW + f0 * 128 + 4 * lane;
-        *reinterpret_cast<uint2*>(l0h + o0) = make_uint2(0u, 0u);
-        *reinterpret_cast<uint2*>(l0l + o0) = make_uint2(0u, 0u);
-      }
-      continue;
+  const int rr = warp >> 1, r = rb + rr, fw = 32 * (warp & 1);  // this warp's row and first frequency
+  if (r > T0) return;
+  const long row_c = (long)t0off[clip];
+  if (r == T0) {  // the zero row after the clip (and, for clip 0, the one before it)
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int k = 0; k < (clip == 0 ? 2 : 1); ++k) {
+      const long row = k == 0 ? row_c + T0 : row_c - 1;
+      uint4* zh = reinterpret_cast<uint4*>(l0h + row * L0_ROW + fw * 128);
+      uint4* zl = reinterpret_cast<uint4*>(l0l + row * L0_ROW + fw * 128);
+      for (int i = lane; i < 32 * 128 / 8; i += 32) zh[i] = z, zl[i] = z;
     }
-    float x[9];
+    return;
+  }
+  const int g = lane >> 2, tq = lane & 3;
+  // taps 2 tq and 2 tq + 1 of this lane's A columns (all < 9), and tap 8 (columns 8..15: tq == 0 only)
+  const int k0 = 2 * tq, k1 = 2 * tq + 1;
+  const int o0 = (k0 / 3) * XP + k0 % 3, o1 = (k1 / 3) * XP + k1 % 3, o8 = 2 * XP + 2;
+  const float* xrow = &xs[2 * rr][0];
+  const long rowbase = (row_c + r) * L0_ROW;
+  uint32_t* sth = stage + warp * 512;  // this warp's 2 KB: hi words [0, 256), lo words [256, 512)
+  uint32_t* stl = sth + 256;
+#pragma unroll 1
+  for (int m = 0; m < 2; ++m) {
+    const int fa = fw + 16 * m + g, fb = fa + 8;  // this lane's two positions (frequencies)
+    uint32_t ah[4], al[4];
+    {
+      const float xa0 = xrow[o0 + 2 * fa], xa1 = xrow[o1 + 2 * fa];
+      const float xb0 = xrow[o0 + 2 * fb], xb1 = xrow[o1 + 2 * fb];
+      const float xa8 = tq == 0 ? xrow[o8 + 2 * fa] : 0.f, xb8 = tq == 0 ? xrow[o8 + 2 * fb] : 0.f;
+      const float v[4][2] = {{xa0, xa1}, {xb0, xb1}, {xa8, 0.f}, {xb8, 0.f}};
 #pragma unroll
-    for (int kt = 0; kt < 3; ++kt)
-#pragma unroll
-      for (int kf = 0; kf < 3; ++kf) {
-        const int sf = 2 * f0 + kf - 1;
-        x[kt * 3 + kf] = sf >= 0 ? xs[2 * rr + kt][sf] : 0.f;
+      for (int u = 0; u < 4; ++u) {
+        union {
+          __half2 h2;
+          uint32_t w;
+        } H, L;
+        H.h2 = __floats2half2_rn(v[u][0], v[u][1]);
+        const float2 b = __half22float2(H.h2);
+        L.h2 = __floats2half2_rn((v[u][0] - b.x) * kS, (v[u][1] - b.y) * kS);
+        ah[u] = H.w;
+        al[u] = L.w;
       }
-    // the statistics (double) applied in f32: (v - mean) (inv n_c), then ReLU
-    const double2 s2 = mi[task];
-    const float mean_f = (float)s2.x, inv_f = (float)s2.y;
-    float y[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float v = 0.f;
-#pragma unroll
-      for (int k = 0; k < 9; ++k) v = fmaf(x[k], w[j][k], v);
-      y[j] = fmaxf((v - mean_f) * (inv_f * nw[j]), 0.f);
     }
-    uint32_t h01, l01, h23, l23;
-    split2_f16(y[0], y[1], h01, l01);
-    split2_f16(y[2], y[3], h23, l23);
-    *reinterpret_cast<uint2*>(l0h + o) = make_uint2(h01, h23);
-    *reinterpret_cast<uint2*>(l0l + o) = make_uint2(l01, l23);
+    const float2 sa = mi[rr * 64 + fa], sb = mi[rr * 64 + fb];
+#pragma unroll 1
+    for (int nc = 0; nc < 16; nc += 4) {
+      float hh[4][4], xx[4][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int ch = (nc + n) * 8 + g;  // B column of this lane
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(wsh + ch * KP + 2 * tq);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(wsh + ch * KP + 2 * tq + 8);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(wsl + ch * KP + 2 * tq);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(wsl + ch * KP + 2 * tq + 8);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) hh[n][u] = xx[n][u] = 0.f;
+        mma_16816_s(hh[n], ah, bh0, bh1);
+        mma_16816_s(xx[n], ah, bl0, bl1);
+        mma_16816_s(xx[n], al, bh0, bh1);
+      }
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int c = (nc + n) * 8 + 2 * tq;  // this lane's channel pair
+        const float2 nv = *reinterpret_cast<const float2*>(nsm + c);
+        float y[4];
+        y[0] = fmaxf((fmaf(xx[n][0], 1.0f / kS, hh[n][0]) - sa.x) * (sa.y * nv.x), 0.f);
+        y[1] = fmaxf((fmaf(xx[n][1], 1.0f / kS, hh[n][1]) - sa.x) * (sa.y * nv.y), 0.f);
+        y[2] = fmaxf((fmaf(xx[n][2], 1.0f / kS, hh[n][2]) - sb.x) * (sb.y * nv.x), 0.f);
+        y[3] = fmaxf((fmaf(xx[n][3], 1.0f / kS, hh[n][3]) - sb.x) * (sb.y * nv.y), 0.f);
+        uint32_t h01, l01, h23, l23;
+        split2_f16(y[0], y[1], h01, l01);
+        split2_f16(y[2], y[3], h23, l23);
+        // stage [16 positions][32 channels] per plane; 16-byte chunk n of position p at n ^ ((p >> 1) & 3)
+        const int wa = g * 16 + 4 * (n ^ ((g >> 1) & 3)) + tq, wb = wa + 8 * 16;  // fb: row g + 8, same swizzle
+        sth[wa] = h01;
+        stl[wa] = l01;
+        sth[wb] = h23;
+        stl[wb] = l23;
+      }
+      __syncwarp();
+      // 64 contiguous bytes (32 channels) per position and plane: 8 positions per store
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int p = 8 * k + (lane >> 2), j = lane & 3;
+        const int w = p * 16 + 4 * (j ^ ((p >> 1) & 3));
+        const long o = rowbase + (long)(fw + 16 * m + p) * 128 + nc * 8 + 8 * j;
+        *reinterpret_cast<uint4*>(l0h + o) = *reinterpret_cast<const uint4*>(sth + w);
+        *reinterpret_cast<uint4*>(l0l + o) = *reinterpret_cast<const uint4*>(stl + w);
+      }
+      __syncwarp();
+    }
   }
 }
 
