@@ -68,6 +68,27 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// P of two keys as fp16 hi / lo words: hi = fp16(p), lo = fp16(p - hi), the
+// same planes as the generic split, with p - hi formed by one
+// mixed-precision FMA per key straight from the packed hi (hi * -1 + p, exact)
+// instead of unpacking hi to f32 and subtracting: the softmax's exponential
+// pass is bound by instruction issue, and this saves two of six instructions
+// per key pair.
+__device__ __forceinline__ void split2_p(float p0, float p1, uint32_t& hw, uint32_t& lw) {
+  asm("{\n"
+      " .reg .f16 h0, h1, m1;\n"
+      " .reg .f32 l0, l1;\n"
+      " cvt.rn.f16x2.f32 %0, %3, %2;\n"
+      " mov.b32 {h0, h1}, %0;\n"
+      " mov.b16 m1, 0xBC00;\n"
+      " fma.rn.f32.f16 l0, h0, m1, %2;\n"
+      " fma.rn.f32.f16 l1, h1, m1, %3;\n"
+      " cvt.rn.f16x2.f32 %1, l1, l0;\n"
+      "}"
+      : "=r"(hw), "=r"(lw)
+      : "f"(p0), "f"(p1));
+}
+
 __device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -359,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             p1 = 2 * u + 1 < lim ? p1 : 0.f;
           }
           rp[u & 3] += p0 + p1;
-          split2_f16(p0, p1, hv[u], lv[u]);
+          split2_p(p0, p1, hv[u], lv[u]);
         }
         tmem_st16(s_col + 32 * c, hv);
         tmem_st16(s_col + 32 * c + 16, lv);
