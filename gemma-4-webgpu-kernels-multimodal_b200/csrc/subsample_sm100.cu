@@ -5,8 +5,9 @@
 //
 // Layer 0 (1 -> 128 channels, 3x3 stride 2, channel LayerNorm with weight,
 // ReLU): statistics in double from the nine taps and precomputed weight
-// moments, then one warp per (row, frequency) with lane = 4 channels.  The result
-// is stored as fp16 hi / lo planes [rows][64 freq][128 ch] in which every
+// moments, the 128 channel values of 16 positions as mma.sync products of the
+// taps and the filters (split fp16 operands), the statistics applied in f32.
+// The result is stored as fp16 hi / lo planes [rows][64 freq][128 ch] in which every
 // clip's rows are preceded and followed by a zero row, so a layer-1 tap that
 // leaves the clip reads zeros.
 //
