@@ -112,6 +112,32 @@ def test_audio_ragged_batch_matches_single(aud, syn):
         assert np.array_equal(single[0], batch[i]), i
 
 
+def test_audio_layer_tiny_packed_clips(aud, oracle, syn):
+    """One conformer layer on ten packed clips of 1 to 13 encoder rows: the
+    light conv's causal window (its 8-row groups span several clips here) and
+    the chunked attention restart at every clip boundary.  Each clip against
+    the oracle's layer on that clip alone (or the float64
+    envelope), and the packed run against the device's run of the clip alone,
+    bitwise."""
+    import np_ref
+    from conftest import assert_float64_envelope
+    c, W, _ = aud
+    pre = oracle.preprocess_audio(syn.audio_samples(30, 48000), pad_to_multiple_of=None)
+    h, _ = oracle.audio_subsample(W, pre["inputFeatures"], pre["inputFeaturesMask"])
+    rows = [1, 2, 3, 4, 5, 7, 8, 9, 13, 1]
+    assert h.shape[0] >= sum(rows)
+    h = np.ascontiguousarray(h[: sum(rows)], dtype=np.float32)
+    got = c.audio_layers(h, rows, 0, 1)
+    r0 = 0
+    for n in rows:
+        hc = h[r0:r0 + n]
+        assert_float64_envelope(oracle.audio_layer(W, 0, hc), got[r0:r0 + n], np_ref.audio_layer(W, 0, hc),
+                                f"audio layer 0, {n}-row clip at row {r0}")
+        single = c.audio_layers(hc, [n], 0, 1)
+        assert np.array_equal(single, got[r0:r0 + n]), (n, r0)
+        r0 += n
+
+
 def test_audio_errors_and_cap(aud, native, syn, oracle):
     c, W, _ = aud
     with pytest.raises(native.G4MError) as e:
