@@ -11,17 +11,6 @@
 
 namespace g4m {
 
-__device__ __forceinline__ float warp_sum_a(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max_a(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
 // ---------------------------------------------------------------------------
 // Log-mel front end: preprocessGemma4AudioSamples (src/preprocess/audio.ts:22-118)
 // for unpadded clips: periodic Hann window (320), zero-padded radix-2 FFT
